@@ -1,0 +1,277 @@
+// Dispatch layout (sglang moe_align_block_size) and row permutation, on the device.
+//
+// Reference: glm52/reference.py:85-128 (a host loop over experts with .tolist() syncs;
+// bench_layer.py:14-17 keeps it out of the timed region). Contract in
+// glm52/kernels/REFERENCES.md:41-51:
+//   sorted_token_ids : flat (token*topk+k) indices, stably sorted by expert, each
+//                      expert's run padded to a multiple of block_m with `numel`
+//   expert_ids[b]    : expert owning block b
+//   ntp[0]           : padded total
+//
+// Here it is a counting sort. A stable rank of every element among the elements with
+// the same expert and a smaller flat index is built chunk by chunk: inside a warp with
+// __match_any_sync (rank = peers below me), across the 32 warps of a chunk with a
+// per-expert exclusive scan over warp counts. Then
+//   pos(i) = start[expert(i)] + rank(i),
+// which reproduces torch.argsort(stable=True) + the padded placement bit for bit.
+// Small inputs run in one CTA (one launch); large inputs use three launches
+// (per-chunk ranks + histograms, one-CTA scan, scatter) with a global workspace.
+#include "common.cuh"
+#include "host_util.h"
+
+namespace fus {
+
+constexpr int kAlignThreads = 1024;
+constexpr int kAlignWarps = kAlignThreads / 32;
+constexpr int kAlignSmallMax = 8192;   // elements handled by the single-CTA path
+constexpr int kAlignMaxE = 512;
+
+// Ranks the (up to 1024) elements [base, base+1024) of `ids` against each other and
+// against earlier chunks (`cursor[e]` = elements of expert e already ranked).
+// wcnt is [32][E] shared scratch. Returns (through rank_out) the stable rank, -1 for
+// elements that are out of range or carry an invalid expert.
+__device__ void rank_chunk(const int* __restrict__ ids, int base, int numel, int E, int* wcnt,
+                           int* cursor, int& my_e, int& my_rank, int* status) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int i = base + tid;
+  int e = -1;
+  if (i < numel) {
+    e = ids[i];
+    if (e < 0 || e >= E) {
+      raise_status(status, FUS_ERR_BAD_EXPERT);
+      e = -1;
+    }
+  }
+  for (int j = tid; j < kAlignWarps * E; j += kAlignThreads) wcnt[j] = 0;
+  __syncthreads();
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int wr = __popc(peers & ((1u << lane) - 1u));
+  if (e >= 0 && wr == 0) wcnt[warp * E + e] = __popc(peers);
+  __syncthreads();
+  for (int x = tid; x < E; x += kAlignThreads) {
+    int run = cursor[x];
+    for (int w = 0; w < kAlignWarps; ++w) {
+      const int c = wcnt[w * E + x];
+      wcnt[w * E + x] = run;
+      run += c;
+    }
+    cursor[x] = run;
+  }
+  __syncthreads();
+  my_e = e;
+  my_rank = e >= 0 ? wcnt[warp * E + e] + wr : -1;
+  __syncthreads();  // wcnt is cleared by the next chunk
+}
+
+// Per-expert padded placement from counts (cnt[e]); writes start[e], ntp, expert_ids
+// and the pad sentinels. Needs E <= blockDim.x * 1 handled by a strided loop + scan.
+__device__ void place_experts(const int* cnt, int* start, int E, int block_m, int numel,
+                              int* sorted_ids, int sorted_cap, int* expert_ids, int blocks_cap,
+                              int* ntp, int* scan_tmp, int* status) {
+  const int tid = threadIdx.x;
+  // exclusive scan of padded counts (E <= 1024: one element per thread)
+  int padded = 0;
+  if (tid < E) padded = (cnt[tid] + block_m - 1) / block_m * block_m;
+  scan_tmp[tid] = padded;
+  __syncthreads();
+  for (int off = 1; off < kAlignThreads; off <<= 1) {
+    const int v = tid >= off ? scan_tmp[tid - off] : 0;
+    __syncthreads();
+    scan_tmp[tid] += v;
+    __syncthreads();
+  }
+  const int incl = scan_tmp[tid];
+  const int total = scan_tmp[kAlignThreads - 1];
+  if (tid < E) start[tid] = incl - padded;
+  if (tid == 0) {
+    ntp[0] = total;
+    if (total > sorted_cap || total / block_m > blocks_cap) raise_status(status, FUS_ERR_CAPACITY);
+  }
+  if (tid < E && padded > 0) {
+    const int s = incl - padded;
+    for (int b = s / block_m; b < (s + padded) / block_m; ++b)
+      if (b < blocks_cap) expert_ids[b] = tid;
+    for (int p = s + cnt[tid]; p < s + padded; ++p)
+      if (p < sorted_cap) sorted_ids[p] = numel;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kAlignThreads)
+    align_small_kernel(const int* __restrict__ ids, int numel, int E, int block_m,
+                       int* __restrict__ sorted_ids, int sorted_cap, int* __restrict__ expert_ids,
+                       int blocks_cap, int* __restrict__ ntp, int* status) {
+  extern __shared__ int sm[];
+  int* wcnt = sm;                            // [32][E]
+  int* cursor = wcnt + kAlignWarps * E;      // [E]
+  int* start = cursor + E;                   // [E]
+  int* scan_tmp = start + E;                 // [1024]
+  int* rank = scan_tmp + kAlignThreads;      // [numel] (stable rank)
+  int* eid = rank + kAlignSmallMax;          // [numel]
+  for (int x = threadIdx.x; x < E; x += kAlignThreads) cursor[x] = 0;
+  __syncthreads();
+  for (int base = 0; base < numel; base += kAlignThreads) {
+    int e, r;
+    rank_chunk(ids, base, numel, E, wcnt, cursor, e, r, status);
+    if (base + (int)threadIdx.x < numel) {
+      rank[base + threadIdx.x] = r;
+      eid[base + threadIdx.x] = e;
+    }
+  }
+  __syncthreads();
+  place_experts(cursor, start, E, block_m, numel, sorted_ids, sorted_cap, expert_ids, blocks_cap,
+                ntp, scan_tmp, status);
+  for (int i = threadIdx.x; i < numel; i += kAlignThreads) {
+    const int e = eid[i];
+    if (e < 0) continue;
+    const int p = start[e] + rank[i];
+    if (p < sorted_cap) sorted_ids[p] = i;
+  }
+}
+
+// ---- large inputs: 3 launches ------------------------------------------------------
+// chunk c = elements [c*1024, (c+1)*1024): rank within the chunk, hist[c][E]
+__global__ void __launch_bounds__(kAlignThreads)
+    align_rank_kernel(const int* __restrict__ ids, int numel, int E, int* __restrict__ rank,
+                      int* __restrict__ hist, int* status) {
+  extern __shared__ int sm[];
+  int* wcnt = sm;
+  int* cursor = wcnt + kAlignWarps * E;
+  for (int x = threadIdx.x; x < E; x += kAlignThreads) cursor[x] = 0;
+  __syncthreads();
+  const int base = blockIdx.x * kAlignThreads;
+  int e, r;
+  rank_chunk(ids, base, numel, E, wcnt, cursor, e, r, status);
+  if (base + (int)threadIdx.x < numel) rank[base + threadIdx.x] = r;
+  for (int x = threadIdx.x; x < E; x += kAlignThreads) hist[(long)blockIdx.x * E + x] = cursor[x];
+}
+
+// one CTA: hist[c][e] <- start[e] + sum_{c'<c} hist[c'][e]; placement
+__global__ void __launch_bounds__(kAlignThreads)
+    align_scan_kernel(int* __restrict__ hist, int nchunks, int E, int block_m, int numel,
+                      int* __restrict__ sorted_ids, int sorted_cap, int* __restrict__ expert_ids,
+                      int blocks_cap, int* __restrict__ ntp, int* status) {
+  __shared__ int cnt[kAlignMaxE];
+  __shared__ int start[kAlignMaxE];
+  __shared__ int scan_tmp[kAlignThreads];
+  for (int x = threadIdx.x; x < E; x += kAlignThreads) {
+    int run = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int v = hist[(long)c * E + x];
+      hist[(long)c * E + x] = run;
+      run += v;
+    }
+    cnt[x] = run;
+  }
+  __syncthreads();
+  place_experts(cnt, start, E, block_m, numel, sorted_ids, sorted_cap, expert_ids, blocks_cap, ntp,
+                scan_tmp, status);
+  for (int x = threadIdx.x; x < E; x += kAlignThreads)
+    for (int c = 0; c < nchunks; ++c) hist[(long)c * E + x] += start[x];
+}
+
+__global__ void align_scatter_kernel(const int* __restrict__ ids, int numel, int E,
+                                     const int* __restrict__ rank, const int* __restrict__ hist,
+                                     int* __restrict__ sorted_ids, int sorted_cap) {
+  const int i = blockIdx.x * kAlignThreads + threadIdx.x;
+  if (i >= numel) return;
+  const int e = ids[i];
+  const int r = rank[i];
+  if (e < 0 || e >= E || r < 0) return;
+  const int p = hist[(long)blockIdx.x * E + e] + r;
+  if (p < sorted_cap) sorted_ids[p] = i;
+}
+
+// ---- permutation ------------------------------------------------------------------
+__global__ void permute_rows_kernel(const __nv_bfloat16* __restrict__ src, long ld_src,
+                                    const int* __restrict__ sorted_ids, const int* __restrict__ ntp,
+                                    int div, int num_valid, __nv_bfloat16* __restrict__ dst,
+                                    long ld_dst, int max_rows, int H) {
+  const int rows = min(__ldg(ntp), max_rows);
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const int nv = H >> 3;
+  for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < rows; p += warps) {
+    const int id = __ldg(sorted_ids + p);
+    uint4* d = reinterpret_cast<uint4*>(dst + (long)p * ld_dst);
+    if (id < num_valid) {
+      const uint4* s = reinterpret_cast<const uint4*>(src + (long)(id / div) * ld_src);
+      for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = __ldg(s + v);
+    } else {
+      for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+size_t small_smem_bytes(int E) {
+  return sizeof(int) * ((size_t)kAlignWarps * E + 2 * E + kAlignThreads + 2 * kAlignSmallMax);
+}
+
+}  // namespace fus
+
+using namespace fus;
+
+extern "C" size_t fus_moe_align_workspace(int numel, int E) {
+  if (numel <= kAlignSmallMax) return 0;
+  const size_t nchunks = (size_t)ceil_div(numel, kAlignThreads);
+  return sizeof(int) * ((size_t)numel + nchunks * (size_t)E) + 256;
+}
+
+extern "C" int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids,
+                             int sorted_cap, int* expert_ids, int blocks_cap, int* ntp,
+                             void* workspace, size_t ws_bytes, void* stream, int* status) {
+  if (!ids || !sorted_ids || !expert_ids || !ntp || numel < 0 || block_m < 1)
+    return set_error(FUS_E_INVALID, "moe_align: bad args");
+  if (E < 1 || E > kAlignMaxE) return set_error(FUS_E_UNSUPPORTED, "moe_align: E=%d > %d", E, kAlignMaxE);
+  cudaStream_t st = as_stream(stream);
+  if (numel <= kAlignSmallMax) {
+    const size_t sm = small_smem_bytes(E);
+    static bool attr_done = false;
+    if (!attr_done) {
+      cudaError_t e = cudaFuncSetAttribute(align_small_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)small_smem_bytes(kAlignMaxE));
+      if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "moe_align attr: %s", cudaGetErrorString(e));
+      attr_done = true;
+    }
+    align_small_kernel<<<1, kAlignThreads, sm, st>>>(ids, numel, E, block_m, sorted_ids, sorted_cap,
+                                                    expert_ids, blocks_cap, ntp, status);
+    return check_launch("moe_align_small");
+  }
+  const size_t need = fus_moe_align_workspace(numel, E);
+  if (!workspace || ws_bytes < need || !aligned16(workspace))
+    return set_error(FUS_E_INVALID, "moe_align: workspace of %zu bytes required", need);
+  const int nchunks = ceil_div(numel, kAlignThreads);
+  int* rank = reinterpret_cast<int*>(workspace);
+  int* hist = rank + numel;
+  const size_t sm = sizeof(int) * ((size_t)kAlignWarps * E + E);
+  static bool attr_done2 = false;
+  if (!attr_done2) {
+    cudaError_t e = cudaFuncSetAttribute(align_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(sizeof(int) * ((size_t)kAlignWarps * kAlignMaxE + kAlignMaxE)));
+    if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "moe_align attr: %s", cudaGetErrorString(e));
+    attr_done2 = true;
+  }
+  align_rank_kernel<<<nchunks, kAlignThreads, sm, st>>>(ids, numel, E, rank, hist, status);
+  align_scan_kernel<<<1, kAlignThreads, 0, st>>>(hist, nchunks, E, block_m, numel, sorted_ids,
+                                                 sorted_cap, expert_ids, blocks_cap, ntp, status);
+  align_scatter_kernel<<<nchunks, kAlignThreads, 0, st>>>(ids, numel, E, rank, hist, sorted_ids,
+                                                          sorted_cap);
+  return check_launch("moe_align");
+}
+
+extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
+                                int div, int num_valid, void* dst, long ld_dst, int max_rows, int H,
+                                void* stream, int* status) {
+  (void)status;
+  if (!src || !sorted_ids || !ntp || !dst || div < 1 || H <= 0 || H % 8 || max_rows < 0 ||
+      !aligned16(src) || !aligned16(dst) || ld_src % 8 || ld_dst % 8)
+    return set_error(FUS_E_INVALID, "permute_rows: bad args");
+  if (max_rows == 0) return FUS_OK;
+  int grid = ceil_div(max_rows, 8);
+  const int cap = num_sms() * 8;
+  if (grid > cap) grid = cap;
+  permute_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+      (const __nv_bfloat16*)src, ld_src, sorted_ids, ntp, div, num_valid, (__nv_bfloat16*)dst,
+      ld_dst, max_rows, H);
+  return check_launch("permute_rows");
+}

@@ -1,0 +1,28 @@
+// Host-side helpers shared by the C-ABI translation units: error reporting, launch
+// checks and TMA tensor-map encoding (driver entry point fetched through the runtime,
+// so the library links only against cudart).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/fusion_b200.h"
+
+namespace fus {
+
+// Records a printf-style message retrievable by fus_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+// Turns a pending launch error into FUS_E_LAUNCH.
+int check_launch(const char* what);
+// Encodes a 2D bf16 tensor map with 128-byte swizzle: `inner` contiguous elements per
+// row, `rows` rows, row pitch `ld` elements, box = box_inner x box_rows.
+int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t ld,
+                      uint32_t box_inner, uint32_t box_rows);
+int num_sms();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
+
+}  // namespace fus

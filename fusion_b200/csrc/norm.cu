@@ -1,0 +1,266 @@
+// Memory-bound row kernels of the MoE block: ResAdd+RMSNorm, SwiGLU, expert merge
+// (+ residual + shared expert), residual add and accumulator seeding.
+//
+// All of them stream bf16 rows with 128-bit loads/stores (8 elements per thread per
+// access), keep arithmetic in fp32, and reproduce the reference's rounding points
+// exactly where the reference rounds (glm52/reference.py:22-40, :159-188).
+#include "common.cuh"
+#include "host_util.h"
+
+namespace fus {
+
+// ======================================================================================
+// ResAdd + RMSNorm   (glm52/kernels/add_rmsnorm.py:50-191; reference.py:22-33)
+// One CTA per row; the row stays in registers between the sum of squares and the
+// normalisation, so the fused form moves exactly 2 reads + 2 writes per element.
+// ======================================================================================
+constexpr int kNormThreads = 256;
+
+template <int VPT>
+__global__ void __launch_bounds__(kNormThreads)
+    add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long ldx,
+                       const __nv_bfloat16* __restrict__ res, long ldr,
+                       const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h1,
+                       long ldh, __nv_bfloat16* __restrict__ out, long ldo, int N, float eps,
+                       int do_add, int do_norm) {
+  const int t = blockIdx.x;
+  const int nv = N >> 3;
+  float h[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int idx = threadIdx.x + v * kNormThreads;
+    if (idx < nv) {
+      unpack8(ldg_stream(x + (long)t * ldx + idx * 8), h[v]);
+      if (do_add) {
+        float r[8];
+        unpack8(ldg_stream(res + (long)t * ldr + idx * 8), r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[v][e] = round_bf(h[v][e] + r[e]);  // h1 = bf16(x + r)
+        if (h1) *reinterpret_cast<uint4*>(h1 + (long)t * ldh + idx * 8) = pack8(h[v]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += h[v][e] * h[v][e];
+    }
+  }
+  if (!do_norm) return;
+
+  __shared__ float red[kNormThreads / 32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < kNormThreads / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float mean = red[0] / (float)N;
+  const float rstd = 1.0f / sqrtf(mean + eps);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int idx = threadIdx.x + v * kNormThreads;
+    if (idx < nv) {
+      float g[8], o[8];
+      unpack8(*reinterpret_cast<const uint4*>(w + idx * 8), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = round_bf(h[v][e] * rstd) * g[e];  // (h*rstd).bf16 * w
+      *reinterpret_cast<uint4*>(out + (long)t * ldo + idx * 8) = pack8(o);
+    }
+  }
+}
+
+// ======================================================================================
+// SwiGLU  (glm52/kernels/moe_gateup.py:154-182; reference.py:36-40)
+// ======================================================================================
+__global__ void silu_and_mul_kernel(const __nv_bfloat16* __restrict__ x, long ldx,
+                                    __nv_bfloat16* __restrict__ y, long ldy, int I) {
+  const int m = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= I) return;
+  float g[8], u[8], o[8];
+  unpack8(ldg_stream(x + (long)m * ldx + c), g);
+  unpack8(ldg_stream(x + (long)m * ldx + I + c), u);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + expf(-g[e]))) * u[e];
+  *reinterpret_cast<uint4*>(y + (long)m * ldy + c) = pack8(o);
+}
+
+// ======================================================================================
+// Expert merge (+ residual, + shared expert)
+//   (glm52/kernels/merge_resadd.py:59-185, moe_down_merge.py:300-349, reference.py:159-188)
+// ======================================================================================
+template <int KT>
+__global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, long ld_k, int K,
+                             const float* __restrict__ w, long ldw,
+                             const __nv_bfloat16* __restrict__ res, long ldr,
+                             const __nv_bfloat16* __restrict__ extra, long lde,
+                             __nv_bfloat16* __restrict__ out, long ldo, int H, int round_mid) {
+  const int t = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= H) return;
+  const int nk = KT > 0 ? KT : K;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  const __nv_bfloat16* yt = y + (long)t * ld_t + c;
+  if (KT > 0) {
+    uint4 yv[KT > 0 ? KT : 1];
+#pragma unroll
+    for (int k = 0; k < (KT > 0 ? KT : 1); ++k) yv[k] = ldg_stream(yt + (long)k * ld_k);
+#pragma unroll
+    for (int k = 0; k < (KT > 0 ? KT : 1); ++k) {
+      const float wk = w ? __ldg(w + (long)t * ldw + k) : 1.0f;
+      float f[8];
+      unpack8(yv[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += wk * f[e];
+    }
+  } else {
+    for (int k = 0; k < nk; ++k) {
+      const float wk = w ? __ldg(w + (long)t * ldw + k) : 1.0f;
+      float f[8];
+      unpack8(ldg_stream(yt + (long)k * ld_k), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += wk * f[e];
+    }
+  }
+  if (round_mid) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = round_bf(acc[e]);
+  }
+  if (res) {
+    float f[8];
+    unpack8(ldg_stream(res + (long)t * ldr + c), f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += f[e];
+  }
+  if (extra) {
+    float f[8];
+    unpack8(ldg_stream(extra + (long)t * lde + c), f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += f[e];
+  }
+  *reinterpret_cast<uint4*>(out + (long)t * ldo + c) = pack8(acc);
+}
+
+__global__ void add_kernel(const __nv_bfloat16* __restrict__ a, long lda,
+                           const __nv_bfloat16* __restrict__ b, long ldb,
+                           __nv_bfloat16* __restrict__ o, long ldo, int N) {
+  const int m = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= N) return;
+  float fa[8], fb[8];
+  unpack8(ldg_stream(a + (long)m * lda + c), fa);
+  unpack8(ldg_stream(b + (long)m * ldb + c), fb);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) fa[e] += fb[e];
+  *reinterpret_cast<uint4*>(o + (long)m * ldo + c) = pack8(fa);
+}
+
+__global__ void seed_kernel(__nv_bfloat16* __restrict__ o, long ldo,
+                            const __nv_bfloat16* __restrict__ s, long lds, int N) {
+  const int m = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= N) return;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (s) v = ldg_stream(s + (long)m * lds + c);
+  *reinterpret_cast<uint4*>(o + (long)m * ldo + c) = v;
+}
+
+}  // namespace fus
+
+using namespace fus;
+typedef __nv_bfloat16 bf16;
+
+static bool rows_ok(const void* p, long ld) { return p && aligned16(p) && ld % 8 == 0; }
+
+extern "C" int fus_add_rmsnorm(const void* x, long ldx, const void* res, long ldr, const void* w,
+                               void* h1, long ldh, void* out, long ldo, int T, int N, float eps,
+                               int do_add, int do_norm, void* stream, int* status) {
+  (void)status;
+  if (T < 0 || N <= 0 || N % 8) return set_error(FUS_E_INVALID, "add_rmsnorm: N=%d must be a multiple of 8", N);
+  if (N > kNormThreads * 8 * 8) return set_error(FUS_E_UNSUPPORTED, "add_rmsnorm: N=%d > 16384", N);
+  if (!do_add && !do_norm) return FUS_OK;
+  if (!rows_ok(x, ldx)) return set_error(FUS_E_INVALID, "add_rmsnorm: x rows must be 16-byte aligned");
+  if (do_add && (!rows_ok(res, ldr) || (h1 && !rows_ok(h1, ldh))))
+    return set_error(FUS_E_INVALID, "add_rmsnorm: residual / h1 rows must be 16-byte aligned");
+  if (do_add && !do_norm && !h1) return set_error(FUS_E_INVALID, "add_rmsnorm: add_only needs h1");
+  if (do_norm && (!rows_ok(out, ldo) || !w || !aligned16(w)))
+    return set_error(FUS_E_INVALID, "add_rmsnorm: out / w must be 16-byte aligned");
+  if (T == 0) return FUS_OK;
+  const int vpt = ceil_div(N / 8, kNormThreads);
+  cudaStream_t st = as_stream(stream);
+#define FUS_NORM_LAUNCH(V)                                                                     \
+  add_rmsnorm_kernel<V><<<T, kNormThreads, 0, st>>>(                                          \
+      (const bf16*)x, ldx, (const bf16*)res, ldr, (const bf16*)w, (bf16*)h1, ldh, (bf16*)out, \
+      ldo, N, eps, do_add, do_norm)
+  switch (vpt) {
+    case 1: FUS_NORM_LAUNCH(1); break;
+    case 2: FUS_NORM_LAUNCH(2); break;
+    case 3: FUS_NORM_LAUNCH(3); break;
+    case 4: FUS_NORM_LAUNCH(4); break;
+    default: FUS_NORM_LAUNCH(8); break;
+  }
+#undef FUS_NORM_LAUNCH
+  return check_launch("add_rmsnorm");
+}
+
+static dim3 row_grid(int M, int N, int threads) { return dim3(ceil_div(N / 8, threads), M); }
+
+extern "C" int fus_silu_and_mul(const void* x, long ldx, void* y, long ldy, int M, int I,
+                                void* stream, int* status) {
+  (void)status;
+  if (M < 0 || I <= 0 || I % 8 || !rows_ok(x, ldx) || !rows_ok(y, ldy))
+    return set_error(FUS_E_INVALID, "silu_and_mul: bad shape/alignment");
+  if (M == 0) return FUS_OK;
+  silu_and_mul_kernel<<<row_grid(M, I, 128), 128, 0, as_stream(stream)>>>(
+      (const bf16*)x, ldx, (bf16*)y, ldy, I);
+  return check_launch("silu_and_mul");
+}
+
+extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long ldw,
+                         const void* res, long ldr, const void* extra, long lde, void* out,
+                         long ldo, int T, int H, int round_mid, void* stream, int* status) {
+  (void)status;
+  if (T < 0 || H <= 0 || H % 8 || K < 0) return set_error(FUS_E_INVALID, "merge: bad shape");
+  if (K > 0 && (!y || !aligned16(y) || ld_t % 8 || ld_k % 8))
+    return set_error(FUS_E_INVALID, "merge: y rows must be 16-byte aligned");
+  if ((res && !rows_ok(res, ldr)) || (extra && !rows_ok(extra, lde)) || !rows_ok(out, ldo))
+    return set_error(FUS_E_INVALID, "merge: rows must be 16-byte aligned");
+  if (T == 0) return FUS_OK;
+  cudaStream_t st = as_stream(stream);
+  dim3 grid = row_grid(T, H, 128);
+  if (K == 8)
+    merge_kernel<8><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, w, ldw, (const bf16*)res,
+                                          ldr, (const bf16*)extra, lde, (bf16*)out, ldo, H,
+                                          round_mid);
+  else
+    merge_kernel<0><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, w, ldw, (const bf16*)res,
+                                          ldr, (const bf16*)extra, lde, (bf16*)out, ldo, H,
+                                          round_mid);
+  return check_launch("merge");
+}
+
+extern "C" int fus_add(const void* a, long lda, const void* b, long ldb, void* o, long ldo, int M,
+                       int N, void* stream, int* status) {
+  (void)status;
+  if (M < 0 || N <= 0 || N % 8 || !rows_ok(a, lda) || !rows_ok(b, ldb) || !rows_ok(o, ldo))
+    return set_error(FUS_E_INVALID, "add: bad shape/alignment");
+  if (M == 0) return FUS_OK;
+  add_kernel<<<row_grid(M, N, 128), 128, 0, as_stream(stream)>>>((const bf16*)a, lda,
+                                                                 (const bf16*)b, ldb, (bf16*)o,
+                                                                 ldo, N);
+  return check_launch("add");
+}
+
+extern "C" int fus_seed(void* o, long ldo, const void* src, long lds, int M, int N, int from_src,
+                        void* stream, int* status) {
+  (void)status;
+  if (M < 0 || N <= 0 || N % 8 || !rows_ok(o, ldo) || (from_src && !rows_ok(src, lds)))
+    return set_error(FUS_E_INVALID, "seed: bad shape/alignment");
+  if (M == 0) return FUS_OK;
+  seed_kernel<<<row_grid(M, N, 128), 128, 0, as_stream(stream)>>>(
+      (bf16*)o, ldo, from_src ? (const bf16*)src : nullptr, lds, N);
+  return check_launch("seed");
+}

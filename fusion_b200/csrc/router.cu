@@ -1,0 +1,223 @@
+// Router of the GLM-5.2 MoE block: fp32 logits on the tensor cores, then sigmoid
+// noaux_tc top-k selection.
+//
+// Reference: glm52/reference.py:46-79 (router), glm52/kernels/norm_router.py:347 and
+// :352 (router_gemm / topk_only entry points).
+//
+// Logits. The router weight is fp32 (moe_router_dtype float32). Every fp32 value is
+// exactly the sum of three bf16 values (8+8+8 significand bits), and x2 is bf16, so
+// x2 . W == x2 . W_hi + x2 . W_mid + x2 . W_lo with every product exact in fp32. The
+// three planes are laid along K ([E, 3H]) and accumulated into one fp32 TMEM
+// accumulator by the grouped tcgen05 GEMM, i.e. an fp32-accurate GEMM at bf16
+// tensor-core rate. Small T splits K across CTAs into fp32 partial planes that the
+// top-k kernel sums in a fixed order, so the result is deterministic.
+#include "common.cuh"
+#include "host_util.h"
+
+namespace fus {
+
+__global__ void split_weight_kernel(const float* __restrict__ wg, __nv_bfloat16* __restrict__ wa,
+                                    int E, int H) {
+  const long n = (long)E * H;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    const int e = (int)(i / H), k = (int)(i % H);
+    const float w = wg[i];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+    const float r1 = w - __bfloat162float(hi);
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+    const float r2 = r1 - __bfloat162float(mid);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(r2);
+    __nv_bfloat16* row = wa + (long)e * 3 * H;
+    row[k] = hi;
+    row[H + k] = mid;
+    row[2 * H + k] = lo;
+  }
+}
+
+__global__ void transpose_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out,
+                                 int R, int C) {  // in [R, C] -> out [C, R]
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < R && c < C) tile[i][threadIdx.x] = in[(long)r * C + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < R && c < C) out[(long)c * R + r] = tile[threadIdx.x][i];
+  }
+}
+
+// One warp per token. Lane l owns experts [8l, 8l+8).
+constexpr int kTopkWarps = 8;
+
+__global__ void __launch_bounds__(kTopkWarps * 32)
+    topk_kernel(const float* __restrict__ partial, long split_stride, int nsplit,
+                const float* __restrict__ bias, float* __restrict__ logits_out,
+                float* __restrict__ topw, int* __restrict__ topi, int T, int E, int topk,
+                float scale, int renorm) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kTopkWarps + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int e0 = lane * 8;
+  float l[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) l[j] = 0.f;
+  if (e0 < E) {  // E % 8 == 0 (host check) so a lane's 8 experts are all valid or all not
+    const float* p = partial + (long)t * E + e0;
+    for (int s = 0; s < nsplit; ++s) {
+      const float4 a = *reinterpret_cast<const float4*>(p + (long)s * split_stride);
+      const float4 b = *reinterpret_cast<const float4*>(p + (long)s * split_stride + 4);
+      l[0] += a.x; l[1] += a.y; l[2] += a.z; l[3] += a.w;
+      l[4] += b.x; l[5] += b.y; l[6] += b.z; l[7] += b.w;
+    }
+    if (logits_out) {
+      float4* o = reinterpret_cast<float4*>(logits_out + (long)t * E + e0);
+      o[0] = make_float4(l[0], l[1], l[2], l[3]);
+      o[1] = make_float4(l[4], l[5], l[6], l[7]);
+    }
+  }
+  float sc[8], ch[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = e0 + j;
+    if (e < E) {
+      sc[j] = 1.0f / (1.0f + expf(-l[j]));
+      ch[j] = sc[j] + (bias ? __ldg(bias + e) : 0.f);
+    } else {
+      sc[j] = 0.f;
+      ch[j] = -INFINITY;
+    }
+  }
+  unsigned used = 0;
+  float my_w = 0.f;
+  int my_id = 0;
+  float wsum = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (!(used & (1u << j)) && e0 + j < E && (ch[j] > bv || bi == 0x7fffffff)) {
+        bv = ch[j];
+        bi = e0 + j;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    const int owner = bi >> 3;
+    float s_win = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (lane == owner && bi == e0 + j) {
+        used |= 1u << j;
+        s_win = sc[j];
+      }
+    s_win = __shfl_sync(0xffffffffu, s_win, owner & 31);
+    wsum += s_win;
+    if (lane == k) {
+      my_w = s_win;
+      my_id = bi;
+    }
+  }
+  if (lane < topk) {
+    float wv = my_w;
+    if (renorm) wv = wv / fmaxf(wsum, 1e-20f);
+    wv = wv * scale;
+    topw[(long)t * topk + lane] = wv;
+    topi[(long)t * topk + lane] = my_id;
+  }
+}
+
+int router_block_n(int T) {
+  return T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+}
+
+}  // namespace fus
+
+using namespace fus;
+
+extern "C" int fus_router_split_weight(const float* wg, void* wa, int E, int H, void* stream) {
+  if (!wg || !wa || E <= 0 || H <= 0) return set_error(FUS_E_INVALID, "split_weight: bad args");
+  const long n = (long)E * H;
+  const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  split_weight_kernel<<<grid, 256, 0, as_stream(stream)>>>(wg, (__nv_bfloat16*)wa, E, H);
+  return check_launch("router_split_weight");
+}
+
+extern "C" int fus_router_transpose_weight(const void* wgt, void* wa, int H, int E, void* stream) {
+  if (!wgt || !wa || E <= 0 || H <= 0) return set_error(FUS_E_INVALID, "transpose_weight: bad args");
+  dim3 grid(ceil_div(E, 32), ceil_div(H, 32));
+  transpose_kernel<<<grid, dim3(32, 8), 0, as_stream(stream)>>>((const __nv_bfloat16*)wgt,
+                                                                (__nv_bfloat16*)wa, H, E);
+  return check_launch("router_transpose_weight");
+}
+
+extern "C" int fus_router_nsplit(int T, int H, int E, int nplanes) {
+  if (T <= 0 || H <= 0 || E <= 0 || nplanes <= 0 || H % 64 || E % 128) return 1;
+  const int bn = router_block_n(T);
+  const long units = (long)(E / 128) * ceil_div(T, bn);
+  const int ksteps = nplanes * H / 64;
+  long want = (num_sms() + units - 1) / units;
+  if (want > ksteps / 4) want = ksteps / 4;
+  if (want > 64) want = 64;
+  if (want < 1) want = 1;
+  const int kps = ceil_div(ksteps, want);
+  return ceil_div(ksteps, kps);  // the split count the GEMM will actually use
+}
+
+extern "C" int fus_router_logits(const void* x2, long ldx, const void* wa, int nplanes,
+                                 float* partial, int T, int H, int E, int nsplit, void* stream,
+                                 int* status) {
+  if (!x2 || !wa || !partial || T < 0 || nplanes < 1)
+    return set_error(FUS_E_INVALID, "router_logits: bad args");
+  if (E % 128) return set_error(FUS_E_UNSUPPORTED, "router_logits: E=%d must be a multiple of 128", E);
+  if (H % 64) return set_error(FUS_E_UNSUPPORTED, "router_logits: H=%d must be a multiple of 64", H);
+  if (T == 0) return FUS_OK;
+  const int ksteps = nplanes * H / 64;
+  if (nsplit < 1 || nsplit > ksteps || ceil_div(ksteps, ceil_div(ksteps, nsplit)) != nsplit)
+    return set_error(FUS_E_INVALID, "router_logits: nsplit=%d not normalised (use fus_router_nsplit)",
+                     nsplit);
+  const int bn = router_block_n(T);
+  fus_gemm_group g{};
+  g.w = wa;
+  g.n_experts = 1;
+  g.x = x2;
+  g.ldx = ldx;
+  g.x_rows = T;
+  g.expert_ids = nullptr;
+  g.ntp = nullptr;
+  g.max_blocks = ceil_div(T, bn);
+  g.out = partial;
+  g.ldo = E;
+  g.row_map = nullptr;
+  g.row_limit = T;
+  g.row_scale = nullptr;
+  return fus_grouped_gemm(&g, 1, E, H, nplanes, FUS_EPI_F32, bn, nsplit, (long)T * E, stream,
+                          status);
+}
+
+extern "C" int fus_router_topk(const float* partial, int nsplit, const float* bias,
+                               float* logits_out, float* topw, int* topi, int T, int E, int topk,
+                               float scale, int renorm, void* stream, int* status) {
+  (void)status;
+  if (!partial || !topw || !topi || T < 0 || nsplit < 1)
+    return set_error(FUS_E_INVALID, "router_topk: bad args");
+  if (E <= 0 || E > 256 || E % 8 || topk < 1 || topk > 16 || topk > E)
+    return set_error(FUS_E_UNSUPPORTED, "router_topk: E=%d topk=%d unsupported", E, topk);
+  if (!aligned16(partial) || (logits_out && !aligned16(logits_out)))
+    return set_error(FUS_E_INVALID, "router_topk: logits must be 16-byte aligned");
+  if (T == 0) return FUS_OK;
+  topk_kernel<<<ceil_div(T, kTopkWarps), kTopkWarps * 32, 0, as_stream(stream)>>>(
+      partial, (long)T * E, nsplit, bias, logits_out, topw, topi, T, E, topk, scale, renorm);
+  return check_launch("router_topk");
+}

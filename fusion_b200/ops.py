@@ -1,0 +1,197 @@
+"""Torch-tensor wrappers over the C ABI (device pointers + the current CUDA stream).
+
+PyTorch only supplies device memory and streams here; all arithmetic runs in the
+library's sm_100a kernels. Every wrapper is destination-passing like the C ABI and
+raises ``RuntimeError`` when the library rejects its arguments.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib as L
+
+FUS_EPI_BF16, FUS_EPI_SWIGLU, FUS_EPI_F32 = 0, 1, 2
+ERR_TIMEOUT, ERR_BAD_EXPERT, ERR_CAPACITY = 0x1, 0x2, 0x4
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def status_tensor(device: torch.device | int | None = None) -> torch.Tensor:
+    """The per-device int32 status word the kernels OR error bits into."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    t = _status.get(dev.index)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=dev)
+        _status[dev.index] = t
+    return t
+
+
+def _sp() -> int:
+    return status_tensor().data_ptr()
+
+
+def read_status(clear: bool = True) -> int:
+    """Synchronise and return (then clear) the device status bits."""
+    t = status_tensor()
+    v = int(t.item())
+    if clear and v:
+        t.zero_()
+    return v
+
+
+def check_status() -> None:
+    v = read_status()
+    if v:
+        names = [n for b, n in ((ERR_TIMEOUT, "timeout"), (ERR_BAD_EXPERT, "bad expert id"),
+                                (ERR_CAPACITY, "capacity")) if v & b]
+        raise RuntimeError(f"device status {v:#x}: {', '.join(names)}")
+
+
+def _ld(t: torch.Tensor) -> int:
+    assert t.dim() >= 2 and t.stride(-1) == 1, "rows must be contiguous"
+    return t.stride(-2)
+
+
+# -------------------------------------------------------------------------------------
+def add_rmsnorm(x, res, w, h1, out, eps: float = 1e-5, do_add: bool = True, do_norm: bool = True):
+    T, N = x.shape
+    L.call("fus_add_rmsnorm", _p(x), _ld(x), _p(res), _ld(res) if res is not None else 0, _p(w),
+           _p(h1), _ld(h1) if h1 is not None else 0, _p(out), _ld(out) if out is not None else 0,
+           T, N, eps, int(do_add), int(do_norm), _stream(), _sp())
+
+
+def router_split_weight(wg: torch.Tensor) -> torch.Tensor:
+    """fp32 [E, H] -> bf16 planes [E, 3H] (hi | mid | lo)."""
+    E, H = wg.shape
+    wa = torch.empty(E, 3 * H, dtype=torch.bfloat16, device=wg.device)
+    L.call("fus_router_split_weight", _p(wg.contiguous()), _p(wa), E, H, _stream())
+    return wa
+
+
+def router_transpose_weight(wgt: torch.Tensor) -> torch.Tensor:
+    """bf16 [H, E] -> bf16 [E, H]."""
+    H, E = wgt.shape
+    wa = torch.empty(E, H, dtype=torch.bfloat16, device=wgt.device)
+    L.call("fus_router_transpose_weight", _p(wgt.contiguous()), _p(wa), H, E, _stream())
+    return wa
+
+
+def router_nsplit(T: int, H: int, E: int, nplanes: int) -> int:
+    return int(L.lib().fus_router_nsplit(T, H, E, nplanes))
+
+
+def router_logits(x2, wa, nplanes: int, partial, nsplit: int):
+    T, H = x2.shape
+    E = wa.shape[0]
+    L.call("fus_router_logits", _p(x2), _ld(x2), _p(wa), nplanes, _p(partial), T, H, E, nsplit,
+           _stream(), _sp())
+
+
+def router_topk(partial, nsplit: int, bias, logits_out, topw, topi, scale: float = 2.5,
+                renorm: bool = True):
+    T, topk = topi.shape
+    E = partial.shape[-1]
+    L.call("fus_router_topk", _p(partial), nsplit, _p(bias), _p(logits_out), _p(topw), _p(topi),
+           T, E, topk, scale, int(renorm), _stream(), _sp())
+
+
+def moe_align_workspace(numel: int, E: int) -> int:
+    return int(L.lib().fus_moe_align_workspace(numel, E))
+
+
+def moe_align(ids, E: int, block_m: int, sorted_ids, expert_ids, ntp, workspace=None):
+    flat = ids.reshape(-1)
+    assert flat.is_contiguous() and flat.dtype == torch.int32
+    need = moe_align_workspace(flat.numel(), E)
+    if need and (workspace is None or workspace.numel() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=ids.device)
+    L.call("fus_moe_align", _p(flat), flat.numel(), E, block_m, _p(sorted_ids), sorted_ids.numel(),
+           _p(expert_ids), expert_ids.numel(), _p(ntp), _p(workspace) if need else None,
+           need, _stream(), _sp())
+
+
+def permute_rows(src, sorted_ids, ntp, div: int, num_valid: int, dst, max_rows: int | None = None):
+    H = src.shape[1]
+    if max_rows is None:
+        max_rows = min(dst.shape[0], sorted_ids.numel())
+    L.call("fus_permute_rows", _p(src), _ld(src), _p(sorted_ids), _p(ntp), div, num_valid, _p(dst),
+           _ld(dst), max_rows, H, _stream(), _sp())
+
+
+def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map=None,
+               row_limit: int, row_scale=None, x_rows: int | None = None) -> L.GemmGroup:
+    """Describe one weight stack + token rows for :func:`grouped_gemm`.
+
+    ``w`` is [n_experts, w_rows, K'] (or [w_rows, K'] for one expert) bf16."""
+    g = L.GemmGroup()
+    g.w = _p(w)
+    g.n_experts = w.shape[0] if w.dim() == 3 else 1
+    g.x = _p(x)
+    g.ldx = _ld(x)
+    g.x_rows = x.shape[0] if x_rows is None else x_rows
+    g.expert_ids = _p(expert_ids)
+    g.ntp = _p(ntp)
+    g.max_blocks = max_blocks
+    g.out = _p(out)
+    g.ldo = _ld(out)
+    g.row_map = _p(row_map)
+    g.row_limit = row_limit
+    g.row_scale = _p(row_scale)
+    return g
+
+
+def grouped_gemm(groups: list[L.GemmGroup], w_rows: int, K: int, epilogue: int, block_n: int,
+                 a_kplanes: int = 1, ksplit: int = 1, split_stride: int = 0):
+    arr = (L.GemmGroup * len(groups))(*groups)
+    L.call("fus_grouped_gemm", arr, len(groups), w_rows, K, a_kplanes, epilogue, block_n, ksplit,
+           split_stride, _stream(), _sp())
+
+
+def silu_and_mul(x, y):
+    M, twoI = x.shape
+    L.call("fus_silu_and_mul", _p(x), _ld(x), _p(y), _ld(y), M, twoI // 2, _stream(), _sp())
+
+
+def merge(y3, w, res, extra, out, round_mid: bool = True):
+    """y3: [T, K, H] view (unit stride along H)."""
+    T, K, H = y3.shape
+    L.call("fus_merge", _p(y3), y3.stride(0), y3.stride(1), K, _p(w),
+           w.stride(0) if w is not None else 0, _p(res), _ld(res) if res is not None else 0,
+           _p(extra), _ld(extra) if extra is not None else 0, _p(out), _ld(out), T, H,
+           int(round_mid), _stream(), _sp())
+
+
+def add(a, b, o):
+    M, N = a.shape
+    L.call("fus_add", _p(a), _ld(a), _p(b), _ld(b), _p(o), _ld(o), M, N, _stream(), _sp())
+
+
+def seed(o, src=None):
+    M, N = o.shape
+    L.call("fus_seed", _p(o), _ld(o), _p(src), _ld(src) if src is not None else 0, M, N,
+           int(src is not None), _stream(), _sp())
+
+
+# -------------------------------------------------------------------------------------
+def synth_fill(t: torch.Tensor, seed: int, mean: float = 0.0, std: float = 1.0, offset: int = 0):
+    """Fill ``t`` (bf16 or fp32, contiguous) with the seeded synthetic stream."""
+    assert t.is_contiguous()
+    dtype = {torch.bfloat16: 0, torch.float32: 1}[t.dtype]
+    if t.is_cuda:
+        L.call("fus_synth_fill", _p(t), dtype, t.numel(), offset, seed, mean, std, _stream())
+    else:
+        L.lib().fus_synth_fill_host(C.c_void_p(t.data_ptr()), dtype, t.numel(), offset, seed,
+                                    mean, std)
+    return t

@@ -1,0 +1,63 @@
+"""Seeded synthetic inputs for the GLM-5.2 MoE block.
+
+Every tensor is one stream of the library's bit-reproducible generator
+(``fus_synth_fill`` on the GPU, ``fus_synth_fill_host`` on the CPU give the same
+bits), so the CPU oracle and the GPU see identical inputs without copying 19 GB of
+expert weights, and the oracle can regenerate just the experts a batch routes to.
+
+Distributions follow the configs: h, r ~ N(0,1) bf16; gamma = 1 + N(0, 0.02) bf16;
+router W_g ~ N(0, 0.02) fp32; e_score_correction_bias ~ N(0, 1e-3) fp32; expert and
+shared weights ~ N(0, 0.02) bf16. "N" is the generator's Irwin-Hall(12) normal.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+# name -> (stream id, mean, std, dtype)
+STREAMS: dict[str, tuple[int, float, float, torch.dtype]] = {
+    "h": (1, 0.0, 1.0, torch.bfloat16),
+    "r": (2, 0.0, 1.0, torch.bfloat16),
+    "gamma": (3, 1.0, 0.02, torch.bfloat16),
+    "gate_w": (4, 0.0, 0.02, torch.float32),
+    "bias": (5, 0.0, 1e-3, torch.float32),
+    "w13": (6, 0.0, 0.02, torch.bfloat16),
+    "w2": (7, 0.0, 0.02, torch.bfloat16),
+    "w13s": (8, 0.0, 0.02, torch.bfloat16),
+    "w2s": (9, 0.0, 0.02, torch.bfloat16),
+}
+
+
+def stream_seed(base_seed: int, name: str) -> int:
+    return base_seed * 1_000_003 + STREAMS[name][0]
+
+
+def fill(t: torch.Tensor, base_seed: int, name: str, offset: int = 0) -> torch.Tensor:
+    _, mean, std, dtype = STREAMS[name]
+    assert t.dtype == dtype, (name, t.dtype, dtype)
+    return ops.synth_fill(t, stream_seed(base_seed, name), mean, std, offset)
+
+
+def make(name: str, shape, base_seed: int, device="cpu", offset: int = 0) -> torch.Tensor:
+    t = torch.empty(*shape, dtype=STREAMS[name][3], device=device)
+    return fill(t, base_seed, name, offset)
+
+
+@dataclass(frozen=True)
+class Dims:
+    H: int = 6144
+    I: int = 2048
+    E: int = 256
+    topk: int = 8
+
+
+def expert_weight(name: str, e: int, dims: Dims, base_seed: int, device="cpu") -> torch.Tensor:
+    """One routed expert's w13 [2I, H] or w2 [H, I], regenerated from its offset in the
+    full [E, ...] stack."""
+    shape = (2 * dims.I, dims.H) if name == "w13" else (dims.H, dims.I)
+    n = shape[0] * shape[1]
+    return make(name, shape, base_seed, device, offset=e * n)

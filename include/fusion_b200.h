@@ -1,0 +1,230 @@
+/*
+ * fusion_b200 — C ABI of the B200 (sm_100a) GLM-5.2 MoE-block hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream; no torch types. Every entry point is
+ * destination-passing (the caller allocates every output and workspace), enqueues
+ * work on `stream` asynchronously and returns 0 on success or a negative FUS_E_*
+ * code when an argument is rejected before anything was launched (the message is
+ * available from fus_last_error()). Device-side problems (a pipeline wait that ran
+ * out of time, an expert id out of range, a layout larger than its buffer) are
+ * reported by OR-ing FUS_ERR_* bits into the optional device word `status`, which
+ * the caller reads after synchronising.
+ *
+ * Reference interfaces (HansonZhang-cuhksz/fusion, glm52/) that each entry point
+ * replaces are cited beside it as file:line.
+ *
+ * Layout conventions (same as the reference, glm52/config.py:61-64):
+ *   activations  [T, H] bf16 row-major, row stride `ld*` in elements
+ *   w13          [E, 2I, H] bf16  (rows [0,I) gate, [I,2I) up)
+ *   w2           [E, H, I]  bf16
+ *   router       [E, H] fp32 (nn.Linear); stored on device as bf16 planes
+ *   topk ids     [T, topk] int32, weights [T, topk] fp32
+ */
+#ifndef FUSION_B200_H
+#define FUSION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* host return codes */
+#define FUS_OK 0
+#define FUS_E_INVALID (-1)     /* bad argument (shape, alignment, null pointer) */
+#define FUS_E_LAUNCH (-2)      /* CUDA reported an error when launching */
+#define FUS_E_UNSUPPORTED (-3) /* shape outside what the kernels implement */
+
+/* device status bits */
+#define FUS_ERR_TIMEOUT 0x1    /* a pipeline wait exceeded its time budget */
+#define FUS_ERR_BAD_EXPERT 0x2 /* an expert id outside [0, E) was seen */
+#define FUS_ERR_CAPACITY 0x4   /* a layout did not fit the buffer it was given */
+
+/* epilogues of fus_grouped_gemm */
+#define FUS_EPI_BF16 0   /* out[row, n] = bf16(acc * scale[row]?)                         */
+#define FUS_EPI_SWIGLU 1 /* out[row, n] = bf16(silu(acc_gate) * acc_up), w rows paired     */
+#define FUS_EPI_F32 2    /* out[row, n] = acc (fp32), optional split-K partial planes      */
+
+int fus_version(void);
+const char* fus_last_error(void);
+int fus_num_sms(void);
+
+/* ---------------------------------------------------------------------------------
+ * ResAdd + RMSNorm (fusion #3).
+ * Replaces glm52/kernels/add_rmsnorm.py:234 fused_add_rmsnorm (do_add=1, do_norm=1),
+ * :239 add_only (do_norm=0) and :244 norm_only (do_add=0, x is h1).
+ *   h1  = bf16(x + res)
+ *   out = bf16( bf16(h1 * rsqrt(mean(h1^2) + eps)) * w )      (reference.py:22-33)
+ * ------------------------------------------------------------------------------- */
+int fus_add_rmsnorm(const void* x, long ldx, const void* res, long ldr, const void* w,
+                    void* h1, long ldh, void* out, long ldo, int T, int N, float eps,
+                    int do_add, int do_norm, void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
+ * Router weights. The router GEMM runs on the tensor cores in bf16 with fp32
+ * accumulation over `nplanes` bf16 planes whose sum is the weight:
+ *   fp32 weight  -> 3 planes hi/mid/lo, exact (every fp32 is the sum of 3 bf16)
+ *   bf16 weight  -> 1 plane
+ * fus_router_split_weight: wg [E,H] fp32 -> wa [E, 3H] bf16 (planes along K).
+ * fus_router_transpose_weight: wgt [H,E] bf16 (the layout of
+ *   glm52/kernels/norm_router.py:251-255 wgt_from_gate) -> wa [E,H] bf16.
+ * ------------------------------------------------------------------------------- */
+int fus_router_split_weight(const float* wg, void* wa, int E, int H, void* stream);
+int fus_router_transpose_weight(const void* wgt, void* wa, int H, int E, void* stream);
+
+/* Router GEMM (glm52/kernels/norm_router.py:347 router_gemm; reference.py:61):
+ * partial[s, t, e] = sum over the s-th K split of x2[t,:] . wa[e, :] (fp32).
+ * Summing the nsplit planes (fus_router_topk does, in fixed order) gives
+ * logits = x2.float() @ W.float().T. Use fus_router_nsplit() for nsplit. */
+int fus_router_nsplit(int T, int H, int E, int nplanes);
+int fus_router_logits(const void* x2, long ldx, const void* wa, int nplanes, float* partial,
+                      int T, int H, int E, int nsplit, void* stream, int* status);
+
+/* Router selection (reference.py:62-79; glm52/kernels/norm_router.py:352 topk_only):
+ *   logits = sum_s partial[s]; s = sigmoid(logits); choice = s + bias (bias may be NULL)
+ *   ids = top-k of choice, descending (ties: lower expert id first)
+ *   w = s[ids]; if renorm: w /= max(sum(w), 1e-20); w *= scale
+ * logits_out (optional) receives the summed logits [T, E]. E <= 256, topk <= 16. */
+int fus_router_topk(const float* partial, int nsplit, const float* bias, float* logits_out,
+                    float* topw, int* topi, int T, int E, int topk, float scale, int renorm,
+                    void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
+ * Dispatch layout (glm52/reference.py:85-128 moe_align_block_size, sglang layout):
+ *   stable sort of the flat (token*topk+k) indices by expert, each expert's run
+ *   padded to a multiple of block_m with the sentinel `numel`;
+ *   expert_ids[b] = expert of block b; ntp[0] = padded total.
+ * sorted_cap >= numel + E*(block_m-1) and blocks_cap >= sorted_cap/block_m are
+ * always enough. Entries past ntp[0] are left untouched. `workspace` of
+ * fus_moe_align_workspace(numel, E) bytes (may be 0 for small numel). E <= 512.
+ * ------------------------------------------------------------------------------- */
+size_t fus_moe_align_workspace(int numel, int E);
+int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids, int sorted_cap,
+                  int* expert_ids, int blocks_cap, int* ntp, void* workspace, size_t ws_bytes,
+                  void* stream, int* status);
+
+/* Row permutation into dispatch order (the A gather `offs_token // top_k` of
+ * glm52/kernels/moe_gateup.py:96-99, done once up front so the GEMM reads dense rows):
+ *   dst[p] = src[sorted_ids[p] / div]  if sorted_ids[p] < num_valid, else zeros,
+ * for p < min(ntp[0], max_rows). H % 8 == 0, 16-byte aligned rows. */
+int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp, int div,
+                     int num_valid, void* dst, long ld_dst, int max_rows, int H, void* stream,
+                     int* status);
+
+/* ---------------------------------------------------------------------------------
+ * Grouped expert GEMM on tcgen05 tensor cores (replaces the Triton grouped GEMMs
+ * glm52/kernels/moe_gateup.py:199 launch_gateup and
+ * glm52/kernels/moe_down_merge.py:427 launch_down).
+ *
+ * Each group is one weight stack and one set of token rows. Token rows are cut into
+ * blocks of `block_n`; block b belongs to expert expert_ids[b]. For every block and
+ * every 128-row weight tile the kernel computes
+ *     acc[n, j] = sum_k w[e, n, k] * x[b*block_n + j, k]
+ * (the weight is the MMA's M side, tokens its N side), then the epilogue writes
+ * output row  r = row_map ? row_map[b*block_n + j] : b*block_n + j  (skipped if
+ * r >= row_limit) with:
+ *   FUS_EPI_BF16   out[r, n]           = bf16(acc * (row_scale ? row_scale[r] : 1))
+ *   FUS_EPI_SWIGLU out[r, n]  n < w_rows/2 = bf16(silu(acc[n]) * acc[n + w_rows/2])
+ *   FUS_EPI_F32    out[s][r, n]        = acc over the s-th of `ksplit` K ranges
+ * The weight's K extent may be `a_kplanes` times the token K (bf16 planes of one
+ * fp32 weight): token columns wrap, so all planes accumulate against the same x.
+ * Requirements: K % 64 == 0, w_rows % 128 == 0, 16-byte aligned rows,
+ * block_n in {16, 32, 64, 128, 256}.
+ * ------------------------------------------------------------------------------- */
+typedef struct fus_gemm_group {
+  const void* w;          /* [n_experts, w_rows, a_kplanes*K] bf16                        */
+  int n_experts;
+  const void* x;          /* token rows [x_rows, K] bf16, row stride ldx elements          */
+  long ldx;
+  int x_rows;
+  const int* expert_ids;  /* per block; NULL: every block uses expert 0                    */
+  const int* ntp;         /* device int, rows of x in use; NULL: x_rows                    */
+  int max_blocks;         /* blocks launched for this group (extra blocks exit at once)    */
+  void* out;              /* output, row stride ldo elements                               */
+  long ldo;
+  const int* row_map;     /* NULL: identity                                                */
+  int row_limit;
+  const float* row_scale; /* optional, FUS_EPI_BF16 only                                   */
+} fus_gemm_group;
+
+int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w_rows, int K, int a_kplanes,
+                     int epilogue, int block_n, int ksplit, long split_stride, void* stream,
+                     int* status);
+
+/* ---------------------------------------------------------------------------------
+ * Element-wise / merge kernels
+ * ------------------------------------------------------------------------------- */
+/* glm52/kernels/moe_gateup.py:251 launch_silu_and_mul; reference.py:36-40:
+ *   y[m, i] = bf16(silu(x[m, i]) * x[m, I + i]) */
+int fus_silu_and_mul(const void* x, long ldx, void* y, long ldy, int M, int I, void* stream,
+                     int* status);
+
+/* Merge (glm52/kernels/merge_resadd.py:243-255, moe_down_merge.py:504 launch_moe_sum,
+ * reference.py:159-188 expert_merge):
+ *   m   = sum_k (w ? w[t,k] : 1) * y[t,k,:]                  (fp32, k in order)
+ *   if round_mid: m = bf16(m)
+ *   out = bf16(m + res[t] + extra[t])      (res / extra optional, fp32 sum)
+ * y rows: y + t*ld_t + k*ld_k. */
+int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long ldw,
+              const void* res, long ldr, const void* extra, long lde, void* out, long ldo, int T,
+              int H, int round_mid, void* stream, int* status);
+
+/* moe_down_merge.py:532 launch_resadd / merge_resadd.py:253 resadd_only:
+ *   o = bf16(a + b) */
+int fus_add(const void* a, long lda, const void* b, long ldb, void* o, long ldo, int M, int N,
+            void* stream, int* status);
+
+/* moe_down_merge.py:551 launch_seed: o = from_src ? src : 0 */
+int fus_seed(void* o, long ldo, const void* src, long lds, int M, int N, int from_src,
+             void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
+ * Whole MoE block (glm52/bench/bench_layer.py:395-481 build_chain without o_proj,
+ * oracle composition bench_layer.py:365-374):
+ *   h1, x2  = add_rmsnorm(h, r, gamma)
+ *   ids, w  = router(x2, W_g, bias)                   (sigmoid, noaux_tc, top-k)
+ *   layout  = moe_align(ids, block_n)
+ *   act     = silu(x2 W13_gate^T) * (x2 W13_up^T)     per routed expert + shared
+ *   y       = act W2^T
+ *   out     = bf16( bf16(sum_k w_k y_k) + h1 + y_shared )
+ * block_n = 0 picks the token tile from T. The workspace holds every intermediate.
+ * ------------------------------------------------------------------------------- */
+typedef struct fus_moe_block_desc {
+  int H, I, E, topk;
+  float eps, routed_scale;
+  int renorm;
+  const void* gamma;  /* [H] bf16                                 */
+  const void* wa;     /* router planes [E, nplanes*H] bf16        */
+  int nplanes;        /* 3 for an fp32 router weight, 1 for bf16  */
+  const float* bias;  /* [E] fp32 e_score_correction_bias or NULL */
+  const void* w13;    /* [E, 2I, H] bf16                          */
+  const void* w2;     /* [E, H, I] bf16                           */
+  const void* w13s;   /* shared expert [2I, H] bf16 or NULL       */
+  const void* w2s;    /* shared expert [H, I] bf16 or NULL        */
+} fus_moe_block_desc;
+
+int fus_moe_block_pick_block_n(int T, int E, int topk);
+size_t fus_moe_block_workspace(const fus_moe_block_desc* d, int T, int block_n);
+int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h, const void* r, int T,
+                          int block_n, void* out, void* h1, float* topw, int* topi,
+                          void* workspace, size_t ws_bytes, void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
+ * Seeded synthetic inputs, bit-identical on the GPU and the host (no reference
+ * counterpart: the reference draws torch.randn on the device, which a CPU oracle
+ * cannot reproduce). Element i of a stream is
+ *   mean + std * z_i,  z_i = (sum of 12 uniform 16-bit draws - 393210) / 65536
+ * (Irwin-Hall approximation of N(0,1)), rounded to the destination type; i runs
+ * from `offset` so any slice (one expert) can be regenerated alone.
+ * dtype 0 = bf16, 1 = fp32.
+ * ------------------------------------------------------------------------------- */
+int fus_synth_fill(void* dst, int dtype, long n, long offset, unsigned long long seed, float mean,
+                   float std, void* stream);
+void fus_synth_fill_host(void* dst, int dtype, long n, long offset, unsigned long long seed,
+                         float mean, float std);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FUSION_B200_H */

@@ -32,6 +32,7 @@ class GemmGroup(C.Structure):
         ("row_map", vp),
         ("row_limit", i32),
         ("row_scale", vp),
+        ("flags", i32),
     ]
 
 
@@ -73,7 +74,8 @@ SIGNATURES: dict[str, tuple] = {
     "fus_permute_rows": (i32, [vp, i64, vp, vp, i32, i32, vp, i64, i32, i32, vp, vp]),
     "fus_grouped_gemm": (i32, [C.POINTER(GemmGroup), i32, i32, i32, i32, i32, i32, i32, i64, vp, vp]),
     "fus_silu_and_mul": (i32, [vp, i64, vp, i64, i32, i32, vp, vp]),
-    "fus_merge": (i32, [vp, i64, i64, i32, vp, i64, vp, i64, vp, i64, vp, i64, i32, i32, i32, vp, vp]),
+    "fus_merge": (i32, [vp, i64, i64, i32, vp, i64, vp, i64, vp, i64, i32, vp, i64, i32, i32, i32, vp,
+                        vp]),
     "fus_add": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, vp, vp]),
     "fus_seed": (i32, [vp, i64, vp, i64, i32, i32, i32, vp, vp]),
     "fus_moe_block_pick_block_n": (i32, [i32, i32, i32]),

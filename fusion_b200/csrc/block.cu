@@ -9,7 +9,14 @@
 //   5 permute                x2, sorted ids  -> xs (rows in dispatch order)
 //   6 w13 GEMM + SwiGLU      routed (xs) and shared (x2) groups in ONE launch -> act
 //   7 w2 GEMM                routed (act) and shared groups in ONE launch     -> y
-//   8 merge                  out = bf16(bf16(sum_k w_k y_k) + h1 + y_shared)
+//   8 merge                  out = bf16(sum_k w_k y_k + h1 + y_shared)
+//
+// Rounding: only at the tensors the block must store in bf16 (x2, act, y) and at the
+// output. Gate/up feed SwiGLU in fp32, the shared output stays fp32 and the routed sum
+// is not rounded before the residual add. This is closer to the reference's exact fp32
+// path (glm52_h200/reference.py moe_mlp_exact_fp32) than its framework chain, which
+// rounds at every kernel boundary; the framework rounding is still available per step
+// (FUS_GEMM_* flags, fus_merge round_mid) for the drop-in unfused entry points.
 //
 // No step needs the host: every data-dependent size (padded total, blocks per expert)
 // stays on the device, so the sequence can be captured in a CUDA graph.
@@ -52,7 +59,7 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   L.off_act = take((size_t)L.cap * I * 2);
   L.off_acts = take((size_t)T * I * 2);
   L.off_y = take((size_t)L.R * H * 2);
-  L.off_ys = take((size_t)T * H * 2);
+  L.off_ys = take((size_t)T * H * 4);  // shared expert output, fp32
   L.total = o + 256;  // base alignment slack
   return true;
 }
@@ -134,6 +141,7 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   g[0].out = act;
   g[0].ldo = I;
   g[0].row_limit = L.cap;
+  g[0].flags = FUS_GEMM_SWIGLU_EXACT;
   g[1].w = d->w13s;
   g[1].n_experts = 1;
   g[1].x = x2;
@@ -143,6 +151,7 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   g[1].out = act_s;
   g[1].ldo = I;
   g[1].row_limit = T;
+  g[1].flags = FUS_GEMM_SWIGLU_EXACT;
   if ((rc = fus_grouped_gemm(g, shared ? 2 : 1, 2 * I, H, 1, FUS_EPI_SWIGLU, block_n, 1, 0, stream,
                              status)))
     return rc;
@@ -154,14 +163,16 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   g[0].ldo = H;
   g[0].row_map = sorted;
   g[0].row_limit = L.R;
+  g[0].flags = 0;
   g[1].w = d->w2s;
   g[1].x = act_s;
   g[1].ldx = I;
   g[1].out = ys;
   g[1].ldo = H;
+  g[1].flags = FUS_GEMM_OUT_F32;  // reference keeps the shared output in fp32
   if ((rc = fus_grouped_gemm(g, shared ? 2 : 1, H, I, 1, FUS_EPI_BF16, block_n, 1, 0, stream, status)))
     return rc;
   // ---- merge + residual + shared ----
-  return fus_merge(y, (long)K * H, H, K, topw, K, h1, H, shared ? ys : nullptr, H, out, H, T, H, 1,
-                   stream, status);
+  return fus_merge(y, (long)K * H, H, K, topw, K, h1, H, shared ? ys : nullptr, H, 1, out, H, T,
+                   H, /*round_mid=*/0, stream, status);
 }

@@ -33,6 +33,7 @@ struct GroupDev {
   long ldo;
   const int* row_map;
   const float* row_scale;
+  int flags;
 };
 
 struct GemmArgs {
@@ -221,6 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(g + 4) = gp[1];
           *reinterpret_cast<float4*>(u) = up[0];
           *reinterpret_cast<float4*>(u + 4) = up[1];
+          if (!(G.flags & FUS_GEMM_SWIGLU_EXACT)) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              g[e] = round_bf(g[e]);
+              u[e] = round_bf(u[e]);
+            }
+          }
 #pragma unroll
           for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + expf(-g[e]))) * u[e];
           *reinterpret_cast<uint4*>(out + (long)row * G.ldo + mt * 64 + q * 8) = pack8(o);
@@ -239,7 +247,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(v + 4) = sp[1];
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[e] *= sc;
-          *reinterpret_cast<uint4*>(out + (long)row * G.ldo + mt * 128 + q * 8) = pack8(v);
+          if (G.flags & FUS_GEMM_OUT_F32) {
+            float4* dp = reinterpret_cast<float4*>(reinterpret_cast<float*>(G.out) +
+                                                   (long)row * G.ldo + mt * 128 + q * 8);
+            dp[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dp[1] = make_float4(v[4], v[5], v[6], v[7]);
+          } else {
+            *reinterpret_cast<uint4*>(out + (long)row * G.ldo + mt * 128 + q * 8) = pack8(v);
+          }
         }
       } else {
         float* out = reinterpret_cast<float*>(G.out) + (long)split * args.split_stride;
@@ -341,8 +356,9 @@ extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w
       return set_error(FUS_E_INVALID, "group %d: bad sizes", g);
     if (G.ldx < K || G.ldx % 8 || ((uintptr_t)G.x % 16) || ((uintptr_t)G.w % 16))
       return set_error(FUS_E_INVALID, "group %d: rows must be 16-byte aligned", g);
-    if (G.ldo < out_cols || ((uintptr_t)G.out % 16) ||
-        (G.ldo % (epilogue == FUS_EPI_F32 ? 4 : 8)))
+    const bool out32 = epilogue == FUS_EPI_F32 ||
+                       (epilogue == FUS_EPI_BF16 && (G.flags & FUS_GEMM_OUT_F32));
+    if (G.ldo < out_cols || ((uintptr_t)G.out % 16) || (G.ldo % (out32 ? 4 : 8)))
       return set_error(FUS_E_INVALID, "group %d: output rows must be 16-byte aligned", g);
     int rc = make_tmap_bf16_2d(&maps[g], G.w, (uint64_t)a_kplanes * K,
                                (uint64_t)G.n_experts * w_rows, (uint64_t)a_kplanes * K, kBK,
@@ -362,6 +378,7 @@ extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w
     D.ldo = G.ldo;
     D.row_map = G.row_map;
     D.row_scale = G.row_scale;
+    D.flags = G.flags;
     units[g] = (long)G.max_blocks * a.m_tiles * a.ksplit;
   }
   if (ngroups == 1) {

@@ -94,7 +94,7 @@ template <int KT>
 __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, long ld_k, int K,
                              const float* __restrict__ w, long ldw,
                              const __nv_bfloat16* __restrict__ res, long ldr,
-                             const __nv_bfloat16* __restrict__ extra, long lde,
+                             const void* __restrict__ extra, long lde, int extra_f32,
                              __nv_bfloat16* __restrict__ out, long ldo, int H, int round_mid) {
   const int t = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -137,7 +137,13 @@ __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, lon
   }
   if (extra) {
     float f[8];
-    unpack8(ldg_stream(extra + (long)t * lde + c), f);
+    if (extra_f32) {
+      const float* ep = reinterpret_cast<const float*>(extra) + (long)t * lde + c;
+      *reinterpret_cast<uint4*>(f) = ldg_stream(ep);
+      *reinterpret_cast<uint4*>(f + 4) = ldg_stream(ep + 4);
+    } else {
+      unpack8(ldg_stream(reinterpret_cast<const __nv_bfloat16*>(extra) + (long)t * lde + c), f);
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] += f[e];
   }
@@ -220,24 +226,26 @@ extern "C" int fus_silu_and_mul(const void* x, long ldx, void* y, long ldy, int 
 }
 
 extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long ldw,
-                         const void* res, long ldr, const void* extra, long lde, void* out,
-                         long ldo, int T, int H, int round_mid, void* stream, int* status) {
+                         const void* res, long ldr, const void* extra, long lde, int extra_f32,
+                         void* out, long ldo, int T, int H, int round_mid, void* stream,
+                         int* status) {
   (void)status;
   if (T < 0 || H <= 0 || H % 8 || K < 0) return set_error(FUS_E_INVALID, "merge: bad shape");
   if (K > 0 && (!y || !aligned16(y) || ld_t % 8 || ld_k % 8))
     return set_error(FUS_E_INVALID, "merge: y rows must be 16-byte aligned");
-  if ((res && !rows_ok(res, ldr)) || (extra && !rows_ok(extra, lde)) || !rows_ok(out, ldo))
+  if ((res && !rows_ok(res, ldr)) || (extra && (!aligned16(extra) || lde % 8)) ||
+      !rows_ok(out, ldo))
     return set_error(FUS_E_INVALID, "merge: rows must be 16-byte aligned");
   if (T == 0) return FUS_OK;
   cudaStream_t st = as_stream(stream);
   dim3 grid = row_grid(T, H, 128);
   if (K == 8)
     merge_kernel<8><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, w, ldw, (const bf16*)res,
-                                          ldr, (const bf16*)extra, lde, (bf16*)out, ldo, H,
+                                          ldr, extra, lde, extra_f32, (bf16*)out, ldo, H,
                                           round_mid);
   else
     merge_kernel<0><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, w, ldw, (const bf16*)res,
-                                          ldr, (const bf16*)extra, lde, (bf16*)out, ldo, H,
+                                          ldr, extra, lde, extra_f32, (bf16*)out, ldo, H,
                                           round_mid);
   return check_launch("merge");
 }

@@ -14,6 +14,7 @@ import torch
 from . import _lib as L
 
 FUS_EPI_BF16, FUS_EPI_SWIGLU, FUS_EPI_F32 = 0, 1, 2
+GEMM_OUT_F32, GEMM_SWIGLU_EXACT = 0x1, 0x2
 ERR_TIMEOUT, ERR_BAD_EXPERT, ERR_CAPACITY = 0x1, 0x2, 0x4
 
 _status: dict[int, torch.Tensor] = {}
@@ -131,7 +132,8 @@ def permute_rows(src, sorted_ids, ntp, div: int, num_valid: int, dst, max_rows: 
 
 
 def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map=None,
-               row_limit: int, row_scale=None, x_rows: int | None = None) -> L.GemmGroup:
+               row_limit: int, row_scale=None, x_rows: int | None = None,
+               flags: int = 0) -> L.GemmGroup:
     """Describe one weight stack + token rows for :func:`grouped_gemm`.
 
     ``w`` is [n_experts, w_rows, K'] (or [w_rows, K'] for one expert) bf16."""
@@ -149,6 +151,7 @@ def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map
     g.row_map = _p(row_map)
     g.row_limit = row_limit
     g.row_scale = _p(row_scale)
+    g.flags = flags
     return g
 
 
@@ -165,11 +168,12 @@ def silu_and_mul(x, y):
 
 
 def merge(y3, w, res, extra, out, round_mid: bool = True):
-    """y3: [T, K, H] view (unit stride along H)."""
+    """y3: [T, K, H] view (unit stride along H); extra: bf16 or fp32 [T, H]."""
     T, K, H = y3.shape
     L.call("fus_merge", _p(y3), y3.stride(0), y3.stride(1), K, _p(w),
            w.stride(0) if w is not None else 0, _p(res), _ld(res) if res is not None else 0,
-           _p(extra), _ld(extra) if extra is not None else 0, _p(out), _ld(out), T, H,
+           _p(extra), _ld(extra) if extra is not None else 0,
+           int(extra is not None and extra.dtype == torch.float32), _p(out), _ld(out), T, H,
            int(round_mid), _stream(), _sp())
 
 

@@ -61,3 +61,25 @@ def expert_weight(name: str, e: int, dims: Dims, base_seed: int, device="cpu") -
     shape = (2 * dims.I, dims.H) if name == "w13" else (dims.H, dims.I)
     n = shape[0] * shape[1]
     return make(name, shape, base_seed, device, offset=e * n)
+
+
+def make_block_weights(base_seed: int, dims: Dims = Dims(), device="cuda",
+                       shared: bool = True) -> dict[str, torch.Tensor]:
+    """All block weights of config ``base_seed`` (19.3 GB of expert weights at GLM dims;
+    generated on the device in a few milliseconds)."""
+    d = dims
+    w = {
+        "gamma": make("gamma", (d.H,), base_seed, device),
+        "gate_w": make("gate_w", (d.E, d.H), base_seed, device),
+        "bias": make("bias", (d.E,), base_seed, device),
+        "w13": make("w13", (d.E, 2 * d.I, d.H), base_seed, device),
+        "w2": make("w2", (d.E, d.H, d.I), base_seed, device),
+    }
+    if shared:
+        w["w13s"] = make("w13s", (2 * d.I, d.H), base_seed, device)
+        w["w2s"] = make("w2s", (d.H, d.I), base_seed, device)
+    return w
+
+
+def make_inputs(base_seed: int, T: int, dims: Dims = Dims(), device="cuda"):
+    return make("h", (T, dims.H), base_seed, device), make("r", (T, dims.H), base_seed, device)

@@ -46,6 +46,11 @@ extern "C" {
 #define FUS_EPI_SWIGLU 1 /* out[row, n] = bf16(silu(acc_gate) * acc_up), w rows paired     */
 #define FUS_EPI_F32 2    /* out[row, n] = acc (fp32), optional split-K partial planes      */
 
+/* per-group epilogue flags (fus_gemm_group.flags) */
+#define FUS_GEMM_OUT_F32 0x1      /* FUS_EPI_BF16 writes fp32 instead of bf16                */
+#define FUS_GEMM_SWIGLU_EXACT 0x2 /* SwiGLU on fp32 gate/up; default rounds them to bf16     */
+                                  /* first, as the framework's unfused chain does          */
+
 int fus_version(void);
 const char* fus_last_error(void);
 int fus_num_sms(void);
@@ -125,7 +130,9 @@ int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const 
  * output row  r = row_map ? row_map[b*block_n + j] : b*block_n + j  (skipped if
  * r >= row_limit) with:
  *   FUS_EPI_BF16   out[r, n]           = bf16(acc * (row_scale ? row_scale[r] : 1))
- *   FUS_EPI_SWIGLU out[r, n]  n < w_rows/2 = bf16(silu(acc[n]) * acc[n + w_rows/2])
+ *                  (fp32 with FUS_GEMM_OUT_F32)
+ *   FUS_EPI_SWIGLU out[r, n]  n < w_rows/2 = bf16(silu(g) * u),  g = bf16(acc[n]),
+ *                  u = bf16(acc[n + w_rows/2])  (unrounded with FUS_GEMM_SWIGLU_EXACT)
  *   FUS_EPI_F32    out[s][r, n]        = acc over the s-th of `ksplit` K ranges
  * The weight's K extent may be `a_kplanes` times the token K (bf16 planes of one
  * fp32 weight): token columns wrap, so all planes accumulate against the same x.
@@ -146,6 +153,7 @@ typedef struct fus_gemm_group {
   const int* row_map;     /* NULL: identity                                                */
   int row_limit;
   const float* row_scale; /* optional, FUS_EPI_BF16 only                                   */
+  int flags;              /* FUS_GEMM_* bits                                               */
 } fus_gemm_group;
 
 int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w_rows, int K, int a_kplanes,
@@ -165,10 +173,11 @@ int fus_silu_and_mul(const void* x, long ldx, void* y, long ldy, int M, int I, v
  *   m   = sum_k (w ? w[t,k] : 1) * y[t,k,:]                  (fp32, k in order)
  *   if round_mid: m = bf16(m)
  *   out = bf16(m + res[t] + extra[t])      (res / extra optional, fp32 sum)
- * y rows: y + t*ld_t + k*ld_k. */
+ * y rows: y + t*ld_t + k*ld_k. `extra` is bf16, or fp32 when extra_f32 != 0 (the
+ * shared expert's unrounded output, glm52_h200/reference.py:294-311). */
 int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long ldw,
-              const void* res, long ldr, const void* extra, long lde, void* out, long ldo, int T,
-              int H, int round_mid, void* stream, int* status);
+              const void* res, long ldr, const void* extra, long lde, int extra_f32, void* out,
+              long ldo, int T, int H, int round_mid, void* stream, int* status);
 
 /* moe_down_merge.py:532 launch_resadd / merge_resadd.py:253 resadd_only:
  *   o = bf16(a + b) */
@@ -187,7 +196,7 @@ int fus_seed(void* o, long ldo, const void* src, long lds, int M, int N, int fro
  *   layout  = moe_align(ids, block_n)
  *   act     = silu(x2 W13_gate^T) * (x2 W13_up^T)     per routed expert + shared
  *   y       = act W2^T
- *   out     = bf16( bf16(sum_k w_k y_k) + h1 + y_shared )
+ *   out     = bf16( sum_k w_k y_k + h1 + y_shared )   (fp32 sum; x2, act, y stored bf16)
  * block_n = 0 picks the token tile from T. The workspace holds every intermediate.
  * ------------------------------------------------------------------------------- */
 typedef struct fus_moe_block_desc {

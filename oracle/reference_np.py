@@ -207,3 +207,22 @@ def moe_block(h, r, gamma, gate_w, bias, get_w13, get_w2, w13_s, w2_s, num_exper
         acc = acc + shared_expert_mlp(x2, w13_s, w2_s)
     return {"h1": h1, "x2": x2, "logits": logits, "topk_weights": tw, "topk_ids": ti,
             "routed": routed, "out": bf16(acc)}
+
+
+def shared_expert_mlp_exact_fp32(x, w13_s, w2_s) -> np.ndarray:
+    """shared_expert_mlp (reference.py:294-311) without its one bf16 rounding of h,
+    i.e. the exact-fp32 twin built from silu_and_mul_exact_fp32 (reference.py:113-120)."""
+    h = x.astype(np.float32) @ w13_s.astype(np.float32).T
+    return (silu_and_mul_exact_fp32(h) @ w2_s.astype(np.float32).T).astype(np.float32)
+
+
+def moe_block_exact_fp32(x2, h1, topk_weights, topk_ids, get_w13, get_w2, w13_s, w2_s,
+                         num_experts: int) -> np.ndarray:
+    """The block's fp32 path from the reference's exact functions: routed experts via
+    moe_mlp_exact_fp32 (reference.py:262-291) + h1 + the exact shared expert, never
+    rounded (x2 / h1 stay the bf16 tensors the block must store). Returns fp32."""
+    acc = moe_mlp_exact_fp32(x2, get_w13, get_w2, topk_weights, topk_ids, num_experts)
+    acc = acc + h1.astype(np.float32)
+    if w13_s is not None:
+        acc = acc + shared_expert_mlp_exact_fp32(x2, w13_s, w2_s)
+    return acc.astype(np.float32)

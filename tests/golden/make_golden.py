@@ -136,9 +136,13 @@ def gen_block_full():
     w2s = synth.make("w2s", (d.H, d.I), seed)
     routed = R.moe_mlp(x2, w13, w2, tw, ti)
     out = (routed.float() + h1.float() + R.shared_expert_mlp(x2, w13s, w2s)).to(BF)
+    # the exact fp32 path: moe_mlp_exact_fp32 + h1 + shared expert with the exact SwiGLU
+    hs = torch.nn.functional.linear(x2.float(), w13s.float())
+    s_exact = torch.nn.functional.linear(R.silu_and_mul_exact_fp32(hs), w2s.float())
+    exact = R.moe_mlp_exact_fp32(x2, w13, w2, tw, ti) + h1.float() + s_exact
     np.savez_compressed(HERE / "block_full_t2.npz", seed=seed, T=T, h1=bits(h1), x2=bits(x2),
                         topk_weights=f32(tw), topk_ids=ti.numpy(), routed=bits(routed),
-                        out=bits(out))
+                        out=bits(out), out_exact=f32(exact))
 
 
 if __name__ == "__main__":

@@ -1,0 +1,147 @@
+"""GPU parity of the whole MoE block (one C-ABI call) against the reference.
+
+Two references, both on identical seeded inputs:
+  * the reference's fp32 path (moe_mlp_exact_fp32 + h1 + exact shared expert): the
+    north-star bar, max-abs error <= 2e-2 * rms(out);
+  * the reference's framework chain (bf16 at every kernel boundary): its own layer
+    check, max-abs / max|ref| <= 5e-2 (glm52/bench/bench_layer.py:573).
+T=2: the reference's own outputs (golden vectors). T=1 and T=32: the CPU oracle.
+T=256 and T=2048: a torch fp32 GPU restatement of the exact path on the block's own
+routing (ids are checked separately against the oracle router)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_from_bits, golden
+from fusion_b200 import ops, synth
+from fusion_b200.block import MoEBlock
+from gpu_util import DEV, finish, to_np
+from oracle import reference_np as O
+
+pytestmark = pytest.mark.gpu
+D = synth.Dims()
+
+
+@pytest.fixture(scope="module")
+def weights_404():
+    w = synth.make_block_weights(404, D, DEV)
+    yield w
+    del w
+    torch.cuda.empty_cache()
+
+
+def make_block(w):
+    return MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w.get("w13s"),
+                    w.get("w2s"))
+
+
+def parity(out: np.ndarray, exact: np.ndarray, bar: float = 2e-2) -> float:
+    """North-star bar against the fp32 path."""
+    rms = float(np.sqrt((exact.astype(np.float64) ** 2).mean()))
+    err = float(np.abs(out.astype(np.float64) - exact).max())
+    assert err <= bar * rms, f"max-abs {err:.4g} > {bar} * rms {rms:.4g}"
+    return err / rms
+
+
+def framework_check(out: np.ndarray, fw: np.ndarray):
+    """The reference's own layer check against its framework chain."""
+    err = float(np.abs(out.astype(np.float64) - fw).max() / np.abs(fw).max())
+    assert err <= 5e-2, err
+
+
+def test_block_t2_golden(weights_404):
+    g = golden("block_full_t2")
+    blk = make_block(weights_404)
+    h, r = synth.make_inputs(404, 2, D, DEV)
+    o = blk(h, r)
+    finish()
+    assert np.array_equal(to_np(o.h1), bf16_from_bits(g["h1"]))
+    assert np.array_equal(o.topi.cpu().numpy(), g["topk_ids"])
+    np.testing.assert_allclose(to_np(o.topw), g["topk_weights"], rtol=2e-5, atol=2e-6)
+    parity(to_np(o.out), g["out_exact"])
+    framework_check(to_np(o.out), bf16_from_bits(g["out"]))
+
+
+def oracle_block(w, h, r):
+    cpu = {k: to_np(v) for k, v in w.items() if k in ("gamma", "gate_w", "bias", "w13s", "w2s")}
+    cache = {}
+
+    def get(name):
+        def f(e):
+            if (name, e) not in cache:
+                cache[(name, e)] = to_np(w[name][e])
+            return cache[(name, e)]
+        return f
+
+    res = O.moe_block(to_np(h), to_np(r), cpu["gamma"], cpu["gate_w"], cpu["bias"], get("w13"),
+                      get("w2"), cpu.get("w13s"), cpu.get("w2s"), D.E)
+    res["exact"] = O.moe_block_exact_fp32(res["x2"], res["h1"], res["topk_weights"],
+                                          res["topk_ids"], get("w13"), get("w2"),
+                                          cpu.get("w13s"), cpu.get("w2s"), D.E)
+    return res
+
+
+@pytest.mark.parametrize("T", [1, 32])
+def test_block_vs_oracle(weights_404, T):
+    blk = make_block(weights_404)
+    h, r = synth.make_inputs(405 + T, T, D, DEV)
+    o = blk(h, r)
+    finish()
+    ref = oracle_block(weights_404, h, r)
+    assert np.array_equal(to_np(o.h1), ref["h1"])
+    assert np.array_equal(o.topi.cpu().numpy(), ref["topk_ids"])
+    parity(to_np(o.out), ref["exact"])
+    framework_check(to_np(o.out), ref["out"])
+
+
+def torch_block_exact(w, x2, h1, topw, topi):
+    """fp32 GPU restatement of the oracle's exact path (moe_block_exact_fp32)."""
+    T, H = x2.shape
+    I = w["w2"].shape[2]
+    out = torch.zeros(T, H, device=DEV)
+    xf = x2.float()
+    for e in torch.unique(topi).tolist():
+        rows, ks = torch.nonzero(topi == e, as_tuple=True)
+        hh = xf[rows] @ w["w13"][e].float().t()
+        a = torch.nn.functional.silu(hh[:, :I]) * hh[:, I:]
+        out.index_add_(0, rows, (a @ w["w2"][e].float().t()) * topw[rows, ks][:, None])
+    hs = xf @ w["w13s"].float().t()
+    s = (torch.nn.functional.silu(hs[:, :I]) * hs[:, I:]) @ w["w2s"].float().t()
+    return out + h1.float() + s
+
+
+@pytest.mark.parametrize("T", [256, 2048])
+def test_block_large_vs_torch_fp32(weights_404, T):
+    blk = make_block(weights_404)
+    h, r = synth.make_inputs(500 + T, T, D, DEV)
+    o = blk(h, r)
+    finish()
+    x2, h1 = O.add_rmsnorm(to_np(h), to_np(r), to_np(weights_404["gamma"]))
+    assert np.array_equal(to_np(o.h1), h1)
+    # ids against the oracle router on rows whose top-9 gaps exceed 1e-5
+    lg = O.router_logits(x2, to_np(weights_404["gate_w"]))
+    ow, oi = O.router_select(lg, to_np(weights_404["bias"]))
+    s = O.sigmoid(lg) + to_np(weights_404["bias"])
+    top = -np.sort(-s, axis=1)[:, :9]
+    sep = np.all(np.diff(-top, axis=1) > 1e-5, axis=1)
+    assert np.array_equal(o.topi.cpu().numpy()[sep], oi[sep])
+    ref = torch_block_exact(weights_404, torch.from_numpy(x2).to(DEV).to(torch.bfloat16),
+                            o.h1, o.topw, o.topi)
+    parity(to_np(o.out), to_np(ref))
+
+
+def test_block_graph_replay_matches_eager(weights_404):
+    blk = make_block(weights_404)
+    T = 8
+    h, r = synth.make_inputs(77, T, D, DEV)
+    eager = blk(h, r)
+    g, hin, rin, outs, _ = blk.capture(T)
+    hin.copy_(h)
+    rin.copy_(r)
+    g.replay()
+    finish()
+    assert torch.equal(outs.out.view(torch.int16), eager.out.view(torch.int16))
+    assert torch.equal(outs.topi, eager.topi)

@@ -109,3 +109,6 @@ def test_full_block_t2_matches_reference():
     assert np.abs(out - ref).max() <= 2e-2 * rms
     # ulps explode near zero (a cancelling sum); count mismatches instead
     assert (ulp_diff_bf16(out, ref) > 1).mean() < 2e-3
+    exact = O.moe_block_exact_fp32(res["x2"], res["h1"], res["topk_weights"], res["topk_ids"],
+                                   get("w13"), get("w2"), w13s, w2s, d.E)
+    np.testing.assert_allclose(exact, g["out_exact"], rtol=1e-4, atol=1e-4)

@@ -16,6 +16,8 @@
 // which reproduces torch.argsort(stable=True) + the padded placement bit for bit.
 // Small inputs run in one CTA (one launch); large inputs use three launches
 // (per-chunk ranks + histograms, one-CTA scan, scatter) with a global workspace.
+#include <mutex>
+
 #include "common.cuh"
 #include "host_util.h"
 
@@ -274,4 +276,55 @@ extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_
       (const __nv_bfloat16*)src, ld_src, sorted_ids, ntp, div, num_valid, (__nv_bfloat16*)dst,
       ld_dst, max_rows, H);
   return check_launch("permute_rows");
+}
+
+// ---- variant that allocates nothing ---------------------------------------------------
+// Scratch for the multi-launch path (stable ranks + per-chunk histograms) lives in a
+// file-scope device array sized for the largest input this variant accepts: numel up to
+// 65536 (T = 8192 tokens at top-8) and up to 512 experts, 393,472 bytes. Every GPU that
+// loads the library holds it until the process exits.
+namespace fus {
+constexpr int kAlignNoAllocMaxNumel = 65536;
+constexpr size_t kAlignNoAllocBytes =
+    sizeof(int) * ((size_t)kAlignNoAllocMaxNumel +
+                   (size_t)(kAlignNoAllocMaxNumel / kAlignThreads) * kAlignMaxE) + 256;
+static __device__ __align__(256) unsigned char g_align_scratch[kAlignNoAllocBytes];
+
+// Host code cannot use g_align_scratch as a device address (on the host the name is only
+// a stand-in); its device address is looked up once per device with that device current.
+constexpr int kMaxDevices = 64;
+static std::mutex g_align_scratch_mu;
+static void* g_align_scratch_ptr[kMaxDevices] = {};
+}  // namespace fus
+
+extern "C" int fus_moe_align_noalloc(const int* ids, int numel, int E, int block_m,
+                                     int* sorted_ids, int sorted_cap, int* expert_ids,
+                                     int blocks_cap, int* ntp, void* stream, int* status) {
+  if (numel < 0 || numel > kAlignNoAllocMaxNumel)
+    return set_error(FUS_E_UNSUPPORTED, "moe_align_noalloc: numel=%d exceeds the built-in "
+                     "scratch limit of %d pairs (T*topk)", numel, kAlignNoAllocMaxNumel);
+  if (E < 1 || E > kAlignMaxE)
+    return set_error(FUS_E_UNSUPPORTED, "moe_align_noalloc: E=%d > %d", E, kAlignMaxE);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "moe_align_noalloc: cudaGetDevice: %s",
+                                         cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(FUS_E_UNSUPPORTED, "moe_align_noalloc: device %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_align_scratch_mu);
+    scratch = g_align_scratch_ptr[dev];
+    if (!scratch) {
+      e = cudaGetSymbolAddress(&scratch, g_align_scratch);
+      if (e != cudaSuccess || !scratch)
+        return set_error(FUS_E_LAUNCH, "moe_align_noalloc: cudaGetSymbolAddress: %s",
+                         cudaGetErrorString(e));
+      g_align_scratch_ptr[dev] = scratch;
+    }
+  }
+  // Every scratch word the kernels read is written earlier in the same call, so the
+  // previous call's contents never need clearing.
+  return fus_moe_align(ids, numel, E, block_m, sorted_ids, sorted_cap, expert_ids, blocks_cap,
+                       ntp, scratch, kAlignNoAllocBytes, stream, status);
 }

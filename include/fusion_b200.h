@@ -109,6 +109,22 @@ int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids
                   int* expert_ids, int blocks_cap, int* ntp, void* workspace, size_t ws_bytes,
                   void* stream, int* status);
 
+/* Same result as fus_moe_align, but the call allocates nothing and takes no workspace.
+ * No counterpart in the reference. It is for callers that cannot allocate device
+ * memory: engines whose memory pool owns nearly all of HBM from start-up (the KV cache
+ * takes what is left, so a later cudaMalloc fails), and callers that cannot pay the
+ * device-wide synchronisation cudaMalloc / cudaFree imply inside a serving loop.
+ * Scratch is a fixed array inside the library (393,472 bytes on every GPU that loads
+ * it, held until the process exits), so the limits are numel <= 65536 (T <= 8192 at
+ * top-8) and E <= 512; larger inputs are rejected with FUS_E_UNSUPPORTED. The first
+ * call on each device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture. All calls on a
+ * device share the array: calls that may overlap on the GPU (different streams, no
+ * ordering between them) race and corrupt each other's layout. */
+int fus_moe_align_noalloc(const int* ids, int numel, int E, int block_m, int* sorted_ids,
+                          int sorted_cap, int* expert_ids, int blocks_cap, int* ntp, void* stream,
+                          int* status);
+
 /* Row permutation into dispatch order (the A gather `offs_token // top_k` of
  * glm52/kernels/moe_gateup.py:96-99, done once up front so the GEMM reads dense rows):
  *   dst[p] = src[sorted_ids[p] / div]  if sorted_ids[p] < num_valid, else zeros,

@@ -234,7 +234,7 @@ def main() -> None:
     pk = traffic.peaks()
 
     def launches_per_step(T: int) -> int:
-        return 8 + (2 if T * dims.topk > 8192 else 0)
+        return 3 if T <= 16 else 8 + (2 if T * dims.topk > 8192 else 0)
 
     def measure(T: int, steps: int, warmup: int) -> dict:
         g, hin, rin, outs, _ = blk.capture(T)
@@ -271,8 +271,9 @@ def main() -> None:
                 "algorithmic_GB": b / 1e9, "GFLOP": f / 1e9}
 
     def kernel_times(T: int, reps: int = 20) -> dict:
-        """Per-kernel CUDA-event durations of the same chain (one event pair per kernel,
-        L2 flushed before each chain)."""
+        """Per-kernel device time: each step of the chain (same kernels as the block) is
+        captured `reps` times back to back in its own CUDA graph and replayed once; the
+        replay's CUDA-event time / reps is the launch's steady-state duration."""
         ch = BlockChain(blk, T)
         h, r = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cuda")
         steps = ch.steps(h, r)
@@ -280,21 +281,30 @@ def main() -> None:
             for _, fn in steps:
                 fn()
         torch.cuda.synchronize()
-        acc = {n: [] for n, _ in steps}
-        for _ in range(reps):
-            flush.zero_()
-            evs = []
-            for n, fn in steps:
+        ops.check_status()
+        out = {}
+        for n, fn in steps:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                fn()
+            torch.cuda.current_stream().wait_stream(s)
+            with torch.cuda.graph(g):
+                for _ in range(reps):
+                    fn()
+            times = []
+            for _ in range(3):
+                flush.zero_()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record()
-                fn()
+                g.replay()
                 b.record()
-                evs.append((n, a, b))
-            torch.cuda.synchronize()
-            for n, a, b in evs:
-                acc[n].append(a.elapsed_time(b))
+                torch.cuda.synchronize()
+                times.append(a.elapsed_time(b) / reps)
+            out[n] = statistics.median(times)
         ops.check_status()
-        return {n: statistics.fmean(v) for n, v in acc.items()}, ch
+        return out, ch
 
     with ClockSampler(local) as clk:
         head = measure(HEADLINE_T, args.steps, max(args.warmup, 3))

@@ -33,6 +33,32 @@ class GemmGroup(C.Structure):
         ("row_limit", i32),
         ("row_scale", vp),
         ("flags", i32),
+        ("live_ids", vp),
+        ("live_limit", i32),
+        ("token_div", i32),
+        ("gather_ids", vp),
+        ("gather_div", i32),
+    ]
+
+
+class MergeSpec(C.Structure):
+    """Mirror of ``fus_merge_spec``."""
+
+    _fields_ = [
+        ("counters", vp),
+        ("parts", i32),
+        ("y", vp),
+        ("ld_t", i64),
+        ("ld_k", i64),
+        ("topk", i32),
+        ("w", vp),
+        ("ldw", i64),
+        ("res", vp),
+        ("ldr", i64),
+        ("extra", vp),
+        ("lde", i64),
+        ("out", vp),
+        ("ldo", i64),
     ]
 
 
@@ -72,8 +98,15 @@ SIGNATURES: dict[str, tuple] = {
     "fus_moe_align_workspace": (sz, [i32, i32]),
     "fus_moe_align": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, sz, vp, vp]),
     "fus_moe_align_noalloc": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp]),
+    "fus_moe_route_small": (i32, [vp, vp, vp, f32, vp, i32, vp, i32, i32, i32, i32, f32, i32, vp, vp,
+                                  vp, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, i32, vp, vp]),
     "fus_permute_rows": (i32, [vp, i64, vp, vp, i32, i32, vp, i64, i32, i32, vp, vp]),
     "fus_grouped_gemm": (i32, [C.POINTER(GemmGroup), i32, i32, i32, i32, i32, i32, i32, i64, vp, vp]),
+    "fus_grouped_gemm_ex": (i32, [C.POINTER(GemmGroup), i32, i32, i32, i32, i32, i32, i32, i64, i32,
+                                  vp, vp]),
+    "fus_grouped_gemm_tiles": (i32, [i32, i32, i32]),
+    "fus_grouped_gemm_merge": (i32, [C.POINTER(GemmGroup), i32, i32, i32, i32, C.POINTER(MergeSpec),
+                                     vp, vp]),
     "fus_silu_and_mul": (i32, [vp, i64, vp, i64, i32, i32, vp, vp]),
     "fus_merge": (i32, [vp, i64, i64, i32, vp, i64, vp, i64, vp, i64, i32, vp, i64, i32, i32, i32, vp,
                         vp]),

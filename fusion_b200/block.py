@@ -65,8 +65,9 @@ class MoEBlock:
         return int(L.lib().fus_moe_block_workspace(ctypes.byref(self.desc), T, block_n))
 
     def _workspace(self, nbytes: int) -> torch.Tensor:
+        # zero once: the block keeps its counters zero between calls
         if self._ws is None or self._ws.numel() < nbytes:
-            self._ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         return self._ws
 
     def alloc_outputs(self, T: int) -> BlockOutputs:
@@ -103,7 +104,7 @@ class MoEBlock:
         h = torch.zeros(T, self.H, dtype=torch.bfloat16, device=self.device)
         r = torch.zeros_like(h)
         outs = self.alloc_outputs(T)
-        ws = torch.empty(self.workspace_bytes(T, block_n), dtype=torch.uint8, device=self.device)
+        ws = torch.zeros(self.workspace_bytes(T, block_n), dtype=torch.uint8, device=self.device)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):

@@ -37,11 +37,16 @@ class BlockChain:
         self.ntp = torch.zeros(1, dtype=torch.int32, device=dev)
         nws = ops.moe_align_workspace(R, E)
         self.align_ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
-        self.xs = torch.empty(cap, H, dtype=bf, device=dev)
+        self.xs = None if T <= 16 else torch.empty(cap, H, dtype=bf, device=dev)
         self.act = torch.empty(cap, I, dtype=bf, device=dev)
         self.act_s = torch.empty(T, I, dtype=bf, device=dev)
         self.y = torch.empty(R, H, dtype=bf, device=dev)
         self.ys = torch.empty(T, H, dtype=torch.float32, device=dev)
+        self.tiles = ops.gemm_tiles(H, ops.FUS_EPI_BF16, bn)
+        self.counters = torch.zeros(T * self.tiles, dtype=torch.int32, device=dev)
+        self.done = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.small = T <= 16 and E <= 256 and E % 2 == 0 and T * K <= 256
+        self.logits = torch.empty(T, E, dtype=torch.float32, device=dev)
         self.outs: BlockOutputs = blk.alloc_outputs(T)
         self.shared = blk.desc.w13s is not None
 
@@ -51,40 +56,68 @@ class BlockChain:
         keep = b._keep
         gamma, bias, w13, w2, w13s, w2s = keep[0], keep[1], keep[2], keep[3], keep[4], keep[5]
 
+        ws = ops.GEMM_W_STREAM if self.R / E <= bn else 0
+        wss = ops.GEMM_W_STREAM if T <= bn else 0
+
         def w13_step():
-            gs = [ops.gemm_group(w13, self.xs, self.act, expert_ids=self.eids, ntp=self.ntp,
-                                 max_blocks=self.max_blocks, row_limit=self.cap,
-                                 flags=ops.GEMM_SWIGLU_EXACT)]
+            if self.small:  # rows gathered by dispatch position inside the GEMM
+                gs = [ops.gemm_group(w13, self.x2, self.act, expert_ids=self.eids, ntp=self.ntp,
+                                     max_blocks=self.max_blocks, row_limit=self.cap,
+                                     flags=ops.GEMM_SWIGLU_EXACT | ws, live_ids=self.sorted,
+                                     live_limit=self.R, gather_ids=self.sorted, gather_div=K)]
+            else:
+                gs = [ops.gemm_group(w13, self.xs, self.act, expert_ids=self.eids, ntp=self.ntp,
+                                     max_blocks=self.max_blocks, row_limit=self.cap,
+                                     flags=ops.GEMM_SWIGLU_EXACT | ws, live_ids=self.sorted,
+                                     live_limit=self.R)]
             if self.shared:
                 gs.append(ops.gemm_group(w13s, self.x2, self.act_s, max_blocks=-(-T // bn),
-                                         row_limit=T, flags=ops.GEMM_SWIGLU_EXACT))
+                                         row_limit=T, flags=ops.GEMM_SWIGLU_EXACT | wss))
             ops.grouped_gemm(gs, 2 * I, H, ops.FUS_EPI_SWIGLU, bn)
 
-        def w2_step():
+        def w2_groups(merge: bool):
+            mf = ops.GEMM_MERGE if merge else 0
             gs = [ops.gemm_group(w2, self.act, self.y, expert_ids=self.eids, ntp=self.ntp,
                                  max_blocks=self.max_blocks, row_map=self.sorted,
-                                 row_limit=self.R)]
+                                 row_limit=self.R, flags=ws | mf, live_ids=self.sorted,
+                                 live_limit=self.R, token_div=K)]
             if self.shared:
                 gs.append(ops.gemm_group(w2s, self.act_s, self.ys, max_blocks=-(-T // bn),
-                                         row_limit=T, flags=ops.GEMM_OUT_F32))
-            ops.grouped_gemm(gs, H, I, ops.FUS_EPI_BF16, bn)
+                                         row_limit=T, flags=ops.GEMM_OUT_F32 | mf | wss))
+            return gs
 
-        return [
-            ("add_rmsnorm", lambda: ops.add_rmsnorm(h, r, gamma, o.h1, self.x2)),
-            ("router_gemm", lambda: ops.router_logits(self.x2, b.wa, b.nplanes, self.partial,
-                                                      self.nsplit)),
-            ("router_topk", lambda: ops.router_topk(self.partial, self.nsplit, bias, None, o.topw,
-                                                    o.topi)),
-            ("moe_align", lambda: ops.moe_align(o.topi, E, bn, self.sorted, self.eids, self.ntp,
-                                                self.align_ws)),
-            ("permute", lambda: ops.permute_rows(self.x2, self.sorted, self.ntp, K, self.R,
-                                                 self.xs, self.cap)),
-            ("w13_swiglu", w13_step),
-            ("w2", w2_step),
-            ("merge", lambda: ops.merge(self.y.view(T, K, H), o.topw, o.h1,
-                                        self.ys if self.shared else None, o.out,
-                                        round_mid=False)),
-        ]
+        def w2_merge_step():  # decode: merge fused into the w2 epilogue
+            ops.grouped_gemm_merge(w2_groups(True), H, I, bn, counters=self.counters,
+                                   y3=self.y.view(T, K, H), w=o.topw, res=o.h1,
+                                   extra=self.ys if self.shared else None, out=o.out,
+                                   parts=K + (1 if self.shared else 0))
+
+        def w2_step():
+            ops.grouped_gemm(w2_groups(False), H, I, ops.FUS_EPI_BF16, bn)
+
+        def merge_step():
+            ops.merge(self.y.view(T, K, H), o.topw, o.h1, self.ys if self.shared else None,
+                      o.out, round_mid=False)
+
+        if self.small:
+            front = [("route_small", lambda: ops.route_small(
+                h, r, gamma, b.wa, b.nplanes, bias, o.h1, self.x2, self.logits, o.topw, o.topi,
+                bn, self.sorted, self.eids, self.ntp, self.done, self.counters))]
+        else:
+            front = [
+                ("add_rmsnorm", lambda: ops.add_rmsnorm(h, r, gamma, o.h1, self.x2)),
+                ("router_gemm", lambda: ops.router_logits(self.x2, b.wa, b.nplanes,
+                                                          self.partial, self.nsplit)),
+                ("router_topk", lambda: ops.router_topk(self.partial, self.nsplit, bias, None,
+                                                        o.topw, o.topi)),
+                ("moe_align", lambda: ops.moe_align(o.topi, E, bn, self.sorted, self.eids,
+                                                    self.ntp, self.align_ws)),
+                ("permute", lambda: ops.permute_rows(self.x2, self.sorted, self.ntp, K, self.R,
+                                                     self.xs, self.cap)),
+            ]
+        if self.small:
+            return front + [("w13_swiglu", w13_step), ("w2_merge", w2_merge_step)]
+        return front + [("w13_swiglu", w13_step), ("w2", w2_step), ("merge", merge_step)]
 
     def run(self, h, r) -> BlockOutputs:
         for _, fn in self.steps(h, r):

@@ -194,13 +194,10 @@ __global__ void permute_rows_kernel(const __nv_bfloat16* __restrict__ src, long 
   const int nv = H >> 3;
   for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < rows; p += warps) {
     const int id = __ldg(sorted_ids + p);
+    if (id >= num_valid) continue;  // dispatch pad: never multiplied, left as is
     uint4* d = reinterpret_cast<uint4*>(dst + (long)p * ld_dst);
-    if (id < num_valid) {
-      const uint4* s = reinterpret_cast<const uint4*>(src + (long)(id / div) * ld_src);
-      for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = __ldg(s + v);
-    } else {
-      for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = make_uint4(0, 0, 0, 0);
-    }
+    const uint4* s = reinterpret_cast<const uint4*>(src + (long)(id / div) * ld_src);
+    for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = __ldg(s + v);
   }
 }
 

@@ -6,10 +6,14 @@
 //   2 router GEMM (tcgen05)  x2, W_g planes  -> fp32 partial logits
 //   3 top-k                  partials, bias  -> topw, topi
 //   4 moe_align              topi            -> sorted ids, expert ids, padded total
-//   5 permute                x2, sorted ids  -> xs (rows in dispatch order)
-//   6 w13 GEMM + SwiGLU      routed (xs) and shared (x2) groups in ONE launch -> act
-//   7 w2 GEMM                routed (act) and shared groups in ONE launch     -> y
+//      (T <= 16: steps 1-4 are ONE launch, fus_moe_route_small)
+//   5 permute (T > 16)       x2, sorted ids  -> xs (rows in dispatch order)
+//   6 w13 GEMM + SwiGLU      routed rows (T <= 16: gathered from x2 by dispatch position
+//                            with TMA gather4; else xs) and the shared expert's x2 -> act
+//   7 w2 GEMM                routed (act) and shared groups in ONE launch -> y, y_shared
 //   8 merge                  out = bf16(sum_k w_k y_k + h1 + y_shared)
+//      (T <= 16: fused into step 7 -- the CTA that lands a token tile's last
+//       contribution writes the output for it)
 //
 // Rounding: only at the tensors the block must store in bf16 (x2, act, y) and at the
 // output. Gate/up feed SwiGLU in fp32, the shared output stays fp32 and the routed sum
@@ -27,8 +31,9 @@ namespace {
 
 struct BlockLayout {
   int R, cap, blocks_cap, max_blocks, nsplit;
+  int tiles;
   size_t off_x2, off_partial, off_sorted, off_eids, off_ntp, off_align, off_xs, off_act, off_acts,
-      off_y, off_ys, total;
+      off_y, off_ys, off_cnt, off_done, total;
 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -50,16 +55,19 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
     return at;
   };
   L.off_x2 = take((size_t)T * H * 2);
-  L.off_partial = take((size_t)L.nsplit * T * E * 4);
+  L.off_partial = take((size_t)(L.nsplit > 1 ? L.nsplit : 1) * T * E * 4);
   L.off_sorted = take((size_t)L.cap * 4);
   L.off_eids = take((size_t)L.blocks_cap * 4);
   L.off_ntp = take(16);
   L.off_align = take(fus_moe_align_workspace(L.R, E));
-  L.off_xs = take((size_t)L.cap * H * 2);
+  L.off_xs = T <= 16 ? 0 : take((size_t)L.cap * H * 2);  // permuted rows (prefill only)
   L.off_act = take((size_t)L.cap * I * 2);
   L.off_acts = take((size_t)T * I * 2);
   L.off_y = take((size_t)L.R * H * 2);
   L.off_ys = take((size_t)T * H * 4);  // shared expert output, fp32
+  L.tiles = fus_grouped_gemm_tiles(H, FUS_EPI_BF16, bn);
+  L.off_cnt = take((size_t)T * L.tiles * 4);  // fused-merge arrival counters
+  L.off_done = take(16);                      // decode front end's ticket
   L.total = o + 256;  // base alignment slack
   return true;
 }
@@ -69,11 +77,16 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
 using namespace fus;
 
 extern "C" int fus_moe_block_pick_block_n(int T, int E, int topk) {
+  // token tile vs. average tokens per expert: decode keeps one narrow block per expert
+  // (weights streamed once, many CTAs); prefill takes wide tiles with two weight tiles
+  // per CTA (block_n >= 64), where padding the last block of each expert costs less
+  // than the extra weight passes of narrow tiles (measured on B200).
   const double per_expert = (double)T * topk / (E > 0 ? E : 1);
-  if (per_expert <= 16) return 16;
-  if (per_expert <= 64) return 32;
-  if (per_expert <= 160) return 64;
-  return 128;
+  if (per_expert <= 12) return 16;
+  if (per_expert <= 24) return 32;
+  if (per_expert <= 48) return 64;
+  if (per_expert <= 128) return 128;
+  return 256;
 }
 
 extern "C" size_t fus_moe_block_workspace(const fus_moe_block_desc* d, int T, int block_n) {
@@ -112,36 +125,67 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   void* act_s = at(L.off_acts);
   void* y = at(L.off_y);
   void* ys = at(L.off_ys);
+  int* counters = reinterpret_cast<int*>(at(L.off_cnt));
+  int* done = reinterpret_cast<int*>(at(L.off_done));
   const bool shared = d->w13s != nullptr;
 
   int rc;
-  if ((rc = fus_add_rmsnorm(h, H, r, H, d->gamma, h1, H, x2, H, T, H, d->eps, 1, 1, stream, status)))
-    return rc;
-  if ((rc = fus_router_logits(x2, H, d->wa, d->nplanes, partial, T, H, E, L.nsplit, stream, status)))
-    return rc;
-  if ((rc = fus_router_topk(partial, L.nsplit, d->bias, nullptr, topw, topi, T, E, K,
-                            d->routed_scale, d->renorm, stream, status)))
-    return rc;
-  if ((rc = fus_moe_align(topi, L.R, E, block_n, sorted, L.cap, eids, L.blocks_cap, ntp, align_ws,
-                          fus_moe_align_workspace(L.R, E), stream, status)))
-    return rc;
-  if ((rc = fus_permute_rows(x2, H, sorted, ntp, K, L.R, xs, H, L.cap, H, stream, status)))
-    return rc;
+  const bool small = T <= 16 && E <= 256 && E % 2 == 0 && T * K <= 256 &&
+                     (d->nplanes == 1 || d->nplanes == 3);
+  if (small) {
+    // decode: norm + router + top-k + layout in one launch; it also clears the merge
+    // counters, so the down projection needs no separate reset
+    if ((rc = fus_moe_route_small(h, r, d->gamma, d->eps, d->wa, d->nplanes, d->bias, T, H, E, K,
+                                  d->routed_scale, d->renorm, h1, x2, partial, topw, topi,
+                                  block_n, sorted, L.cap, eids, L.blocks_cap, ntp, done, counters,
+                                  T * L.tiles, stream, status)))
+      return rc;
+  } else {
+    if ((rc = fus_add_rmsnorm(h, H, r, H, d->gamma, h1, H, x2, H, T, H, d->eps, 1, 1, stream,
+                              status)))
+      return rc;
+    if ((rc = fus_router_logits(x2, H, d->wa, d->nplanes, partial, T, H, E, L.nsplit, stream,
+                                status)))
+      return rc;
+    if ((rc = fus_router_topk(partial, L.nsplit, d->bias, nullptr, topw, topi, T, E, K,
+                              d->routed_scale, d->renorm, stream, status)))
+      return rc;
+    if ((rc = fus_moe_align(topi, L.R, E, block_n, sorted, L.cap, eids, L.blocks_cap, ntp,
+                            align_ws, fus_moe_align_workspace(L.R, E), stream, status)))
+      return rc;
+    if ((rc = fus_permute_rows(x2, H, sorted, ntp, K, L.R, xs, H, L.cap, H, stream, status)))
+      return rc;
+  }
 
+  // weights stream past L2 when a typical expert fills at most one token block
+  const int wstream = (double)L.R / E <= block_n ? FUS_GEMM_W_STREAM : 0;
   fus_gemm_group g[2] = {};
   // ---- w13 + SwiGLU: routed experts over xs, shared expert over x2 ----
   g[0].w = d->w13;
   g[0].n_experts = E;
-  g[0].x = xs;
+  if (small) {
+    // decode: a handful of rows per launch, gathered from x2 by dispatch position
+    // (TMA gather4) instead of a separate permutation pass
+    g[0].x = x2;
+    g[0].x_rows = T;
+    g[0].gather_ids = sorted;
+    g[0].gather_div = K;
+  } else {
+    // prefill: one permutation pass, then dense box loads (gather4 issues one TMA
+    // operation per 4 rows, too many per stage at 128-256 rows)
+    g[0].x = xs;
+    g[0].x_rows = L.cap;
+  }
   g[0].ldx = H;
-  g[0].x_rows = L.cap;
   g[0].expert_ids = eids;
   g[0].ntp = ntp;
   g[0].max_blocks = L.max_blocks;
   g[0].out = act;
   g[0].ldo = I;
   g[0].row_limit = L.cap;
-  g[0].flags = FUS_GEMM_SWIGLU_EXACT;
+  g[0].flags = FUS_GEMM_SWIGLU_EXACT | wstream;
+  g[0].live_ids = sorted;
+  g[0].live_limit = L.R;
   g[1].w = d->w13s;
   g[1].n_experts = 1;
   g[1].x = x2;
@@ -151,28 +195,56 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   g[1].out = act_s;
   g[1].ldo = I;
   g[1].row_limit = T;
-  g[1].flags = FUS_GEMM_SWIGLU_EXACT;
+  g[1].flags = FUS_GEMM_SWIGLU_EXACT | (T <= block_n ? FUS_GEMM_W_STREAM : 0);
   if ((rc = fus_grouped_gemm(g, shared ? 2 : 1, 2 * I, H, 1, FUS_EPI_SWIGLU, block_n, 1, 0, stream,
                              status)))
     return rc;
-  // ---- w2: routed rows scatter to y[flat], shared rows to ys ----
+  // ---- w2: routed rows to y[flat], shared rows to ys (fp32) ----
   g[0].w = d->w2;
   g[0].x = act;
   g[0].ldx = I;
+  g[0].x_rows = L.cap;
+  g[0].gather_ids = nullptr;
   g[0].out = y;
   g[0].ldo = H;
   g[0].row_map = sorted;
   g[0].row_limit = L.R;
-  g[0].flags = 0;
+  g[0].flags = wstream;
+  g[0].token_div = K;
   g[1].w = d->w2s;
   g[1].x = act_s;
   g[1].ldx = I;
   g[1].out = ys;
   g[1].ldo = H;
-  g[1].flags = FUS_GEMM_OUT_F32;  // reference keeps the shared output in fp32
-  if ((rc = fus_grouped_gemm(g, shared ? 2 : 1, H, I, 1, FUS_EPI_BF16, block_n, 1, 0, stream, status)))
-    return rc;
-  // ---- merge + residual + shared ----
-  return fus_merge(y, (long)K * H, H, K, topw, K, h1, H, shared ? ys : nullptr, H, 1, out, H, T,
-                   H, /*round_mid=*/0, stream, status);
+  g[1].flags = FUS_GEMM_OUT_F32 | (T <= block_n ? FUS_GEMM_W_STREAM : 0);
+  g[1].token_div = 1;
+  if (!small) {
+    // prefill: the merge is a bandwidth-bound pass of its own (in GEMM epilogues it
+    // would be serialised behind each CTA's MMAs)
+    if ((rc = fus_grouped_gemm(g, shared ? 2 : 1, H, I, 1, FUS_EPI_BF16, block_n, 1, 0, stream,
+                               status)))
+      return rc;
+    return fus_merge(y, (long)K * H, H, K, topw, K, h1, H, shared ? ys : nullptr, H, 1, out, H, T,
+                     H, /*round_mid=*/0, stream, status);
+  }
+  // decode: the CTA that lands the last contribution of a (token, tile) writes
+  // out = bf16(sum_k w_k y_k + h1 + ys) for it (counters cleared by the front end)
+  g[0].flags |= FUS_GEMM_MERGE;
+  g[1].flags |= FUS_GEMM_MERGE;
+  fus_merge_spec m{};
+  m.counters = counters;
+  m.parts = K + (shared ? 1 : 0);
+  m.y = y;
+  m.ld_t = (long)K * H;
+  m.ld_k = H;
+  m.topk = K;
+  m.w = topw;
+  m.ldw = K;
+  m.res = h1;
+  m.ldr = H;
+  m.extra = shared ? reinterpret_cast<const float*>(ys) : nullptr;
+  m.lde = H;
+  m.out = out;
+  m.ldo = H;
+  return fus_grouped_gemm_merge(g, shared ? 2 : 1, H, I, block_n, &m, stream, status);
 }

@@ -144,6 +144,11 @@ FUS_DEVICE uint64_t policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+FUS_DEVICE uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 FUS_DEVICE uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -156,6 +161,18 @@ FUS_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* m, uint32_t bar, in
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
+// 4 rows (one 128-byte box row each) gathered by row index into consecutive smem rows;
+// the tensor map's box is one row high. Rows past the tensor's extent read zeros.
+FUS_DEVICE void tma_gather4(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int r0,
+                            int r1, int r2, int r3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3),
+      "l"(policy)
       : "memory");
 }
 

@@ -34,6 +34,27 @@ struct GroupDev {
   const int* row_map;
   const float* row_scale;
   int flags;
+  const int* live_ids;
+  int live_limit;
+  int token_div;
+  const int* gather_ids;
+  int gather_div;
+};
+
+struct MergeDev {
+  int* counters;  // null: no fused merge
+  int parts;
+  const __nv_bfloat16* y;
+  long ld_t, ld_k;
+  int topk;
+  const float* w;
+  long ldw;
+  const __nv_bfloat16* res;
+  long ldr;
+  const float* extra;
+  long lde;
+  __nv_bfloat16* out;
+  long ldo;
 };
 
 struct GemmArgs {
@@ -45,34 +66,106 @@ struct GemmArgs {
   int ksteps_per_split;
   int ksplit;
   int m_tiles;           // weight tiles per expert
+  int group_blocks;      // token blocks swept together across all weight tiles
   long split_stride;     // FUS_EPI_F32 partial plane stride (elements)
   int* status;
+  MergeDev mg;
 };
 
-constexpr int kBK = 64;                 // K elements per stage (128 B rows, one swizzle span)
-constexpr int kATileBytes = 128 * kBK * 2;
+constexpr int kBK = 64;                  // K elements per stage (128 B rows, one swizzle span)
+constexpr int kATileBytes = 128 * kBK * 2;  // one 128-row weight tile per stage
 constexpr int kThreads = 192;
 
-template <int BN>
+__host__ __device__ constexpr int pow2_at_least(int v, int p) { return p >= v ? p : pow2_at_least(v, 2 * p); }
+
+// MT = weight tiles (128 rows each) per CTA, all multiplied by the same token tile; each
+// has its own TMEM accumulator. MT=2 halves the token-operand bytes per flop, so the same
+// shared-memory ring covers twice the MMA time (prefill); MT=1 gives more CTAs (decode).
+template <int BN, int MT>
 struct GemmCfg {
-  static constexpr int STAGES = BN <= 16 ? 6 : BN <= 32 ? 5 : BN <= 64 ? 4 : BN <= 128 ? 6 : 4;
+  static constexpr int A_BYTES = MT * kATileBytes;
   static constexpr int B_BYTES = BN * kBK * 2;
-  static constexpr int STAGE_BYTES = kATileBytes + B_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // small tiles: ~110 KB so that two CTAs share an SM; otherwise ~200 KB
+  static constexpr int RING_TARGET = (MT == 1 && BN <= 64) ? 112 * 1024 : 200 * 1024;
+  static constexpr int STAGES = RING_TARGET / STAGE_BYTES > 8 ? 8 : RING_TARGET / STAGE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int TMEM_COLS = pow2_at_least(MT * BN < 32 ? 32 : MT * BN, 32);
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = RING_BYTES + BAR_BYTES + 1024;  // + alignment slack
-  static_assert(RING_BYTES >= BN * 128 * 4, "epilogue staging must fit in the ring");
+  static_assert(RING_BYTES >= BN * 128 * 4 + BN * 4 + 16, "epilogue staging must fit in the ring");
+  static_assert(STAGES >= 2, "pipeline too shallow");
+  static_assert(TMEM_COLS <= 512, "TMEM holds 512 columns");
 };
 
-template <int BN, int EPI>
+// Fused expert merge, run by the 128 epilogue threads after this CTA stored its rows.
+// Per (token, weight tile) a counter collects the contributions (topk routed rows + the
+// shared row); the CTA that lands the last one sums them in a fixed order, adds the
+// residual, writes the block output for the tile's features and re-arms the counter.
+template <int BN, int MT>
+__device__ __noinline__ void fused_merge_tail(const GemmArgs& args, const GroupDev& G,
+                                              uint8_t* scratch, int pos0, int n_live, int mt,
+                                              int et) {
+  const MergeDev& M = args.mg;
+  int* list_n = reinterpret_cast<int*>(scratch);
+  int* list = list_n + 4;
+  __threadfence();  // release: this thread's row stores before its counter update
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (et == 0) *list_n = 0;
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int j = et; j < n_live; j += 128) {
+    const int pos = pos0 + j;
+    const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
+    if (row >= G.row_limit) continue;
+    const int t = row / G.token_div;
+    const int old = atomicAdd(M.counters + (long)t * args.m_tiles + mt, 1);
+    if (old == M.parts - 1) list[atomicAdd(list_n, 1)] = t;
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  __threadfence();  // acquire: the other contributions are visible now
+  const int n = *list_n;
+  constexpr int NF = 128 * MT;  // features of this tile
+  constexpr int NV = NF / 8;
+  const int f0 = mt * NF;
+  for (int it = et; it < n * NV; it += 128) {
+    const int t = list[it / NV];
+    const int f = f0 + (it % NV) * 8;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int k = 0; k < M.topk; ++k) {
+      const float wk = __ldg(M.w + (long)t * M.ldw + k);
+      float yv[8];
+      unpack8(__ldcg(reinterpret_cast<const uint4*>(M.y + (long)t * M.ld_t + (long)k * M.ld_k + f)),
+              yv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += wk * yv[e];
+    }
+    if (M.res) {
+      float r[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(M.res + (long)t * M.ldr + f)), r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += r[e];
+    }
+    if (M.extra) {
+      const float4* ep = reinterpret_cast<const float4*>(M.extra + (long)t * M.lde + f);
+      const float4 a = __ldcg(ep), b = __ldcg(ep + 1);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    *reinterpret_cast<uint4*>(M.out + (long)t * M.ldo + f) = pack8(acc);
+  }
+  for (int i = et; i < n; i += 128) M.counters[(long)list[i] * args.m_tiles + mt] = 0;
+}
+
+template <int BN, int EPI, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap ta0,
                         const __grid_constant__ CUtensorMap ta1,
                         const __grid_constant__ CUtensorMap tb0,
                         const __grid_constant__ CUtensorMap tb1,
                         const __grid_constant__ GemmArgs args) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, MT>;
   constexpr int STAGES = Cfg::STAGES;
 
   // ---- which unit of work is this CTA ------------------------------------------------
@@ -85,8 +178,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const GroupDev& G = args.g[gi];
   const int split = u % args.ksplit;
   u /= args.ksplit;
-  const int mt = u % args.m_tiles;
-  const int blk = u / args.m_tiles;
+  // `group_blocks` consecutive token blocks visit every weight tile before the next
+  // group starts: a group's token rows stay in L2 and same-expert blocks (adjacent in
+  // the dispatch layout) read each weight tile back to back.
+  const int gsz_full = args.group_blocks * args.m_tiles;
+  const int grp = u / gsz_full;
+  const int rem = u - grp * gsz_full;
+  const int gsz = min(args.group_blocks, G.max_blocks - grp * args.group_blocks);
+  const int mt = rem / gsz;
+  const int blk = grp * args.group_blocks + rem % gsz;
   const int rows_used = G.ntp ? __ldg(G.ntp) : G.x_rows;
   if (blk * BN >= rows_used) return;  // uniform across the CTA: nothing allocated yet
   const int expert = G.expert_ids ? __ldg(G.expert_ids + blk) : 0;
@@ -107,16 +207,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const uint32_t sA = smem_u32(smem);
-  const uint32_t sB = sA + STAGES * kATileBytes;
+  const uint32_t sB = sA + STAGES * Cfg::A_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::RING_BYTES);
   const uint32_t bar_full = smem_u32(bars);
   const uint32_t bar_empty = smem_u32(bars + STAGES);
   const uint32_t bar_accum = smem_u32(bars + 2 * STAGES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* n_live_slot = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int pos0 = blk * BN;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -132,58 +234,106 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
     tmem_relinquish();
+    // live token columns of this block: dispatch pads sit at the end of a block
+    int cnt = 0;
+    if (G.live_ids) {
+      for (int j = lane; j < BN; j += 32) cnt += __ldg(G.live_ids + pos0 + j) < G.live_limit;
+    } else if (lane == 0) {
+      cnt = min(BN, G.x_rows - pos0);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0) *n_live_slot = cnt;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int n_live = *n_live_slot;
+  // MMA width: live columns rounded up to the instruction's N granule (16 for M=128)
+  const int n_mma = max(16, (n_live + 15) & ~15);
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      const uint64_t pol_w = policy_evict_first();  // weights: streamed once
-      const uint64_t pol_x = policy_evict_last();   // token rows: re-read by every tile
-      const int b_row = blk * BN;
-      int a_row0, a_row1 = 0;
-      if (EPI == FUS_EPI_SWIGLU) {
-        a_row0 = expert * args.w_rows + mt * 64;
-        a_row1 = expert * args.w_rows + (args.w_rows >> 1) + mt * 64;
-      } else {
-        a_row0 = expert * args.w_rows + mt * 128;
-      }
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % STAGES;
-        const uint32_t r = (uint32_t)(i / STAGES);
-        if (!mbar_wait_bounded(bar_empty + 8 * s, (r & 1u) ^ 1u, abort_flag, args.status)) break;
-        const uint32_t full = bar_full + 8 * s;
-        mbar_arrive_expect_tx(full, Cfg::STAGE_BYTES);
-        const int kk = (kbeg + i) * kBK;
-        const uint32_t a_dst = sA + s * kATileBytes;
-        if (EPI == FUS_EPI_SWIGLU) {
-          tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
-          tma_load_2d(a_dst + kATileBytes / 2, tma_a, full, kk, a_row1, pol_w);
-        } else {
-          tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
+    // ---------------- TMA producer (lane 0; all lanes issue row gathers) ----------------
+    // weights: evict-first when no other token block reads the tile, else normal
+    const uint64_t pol_w = (G.flags & FUS_GEMM_W_STREAM) ? policy_evict_first()
+                                                         : policy_evict_normal();
+    const uint64_t pol_x = policy_evict_last();  // token rows: re-read by every tile
+    // weight rows of the two A sub-tiles (SwiGLU: gate rows, then the matching up rows)
+    const int ebase = expert * args.w_rows;
+    int a_row0, a_row1;
+    if (EPI == FUS_EPI_SWIGLU) {
+      const int half = 64 * MT;  // features per tile
+      a_row0 = ebase + mt * half;
+      a_row1 = ebase + (args.w_rows >> 1) + mt * half;
+    } else {
+      a_row0 = ebase + mt * 128 * MT;
+      a_row1 = a_row0 + 128;
+    }
+    constexpr uint32_t a_half_bytes = (EPI == FUS_EPI_SWIGLU && MT == 1) ? kATileBytes / 2
+                                                                        : kATileBytes;
+    const bool two_a = (EPI == FUS_EPI_SWIGLU) || MT == 2;
+    // gathered token rows: lane l owns 4-row groups l and l+32 (BN <= 256)
+    const bool gather = G.gather_ids != nullptr;
+    int grow[2][4];
+#pragma unroll
+    for (int gq = 0; gq < 2; ++gq)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = (lane + 32 * gq) * 4 + q;
+        int row = G.x_rows;  // past the end: zero fill
+        if (gather && j < BN) {
+          const int id = __ldg(G.gather_ids + pos0 + j);
+          if (id < G.live_limit) row = id / G.gather_div;
         }
-        tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, b_row, pol_x);
+        grow[gq][q] = row;
+      }
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % STAGES;
+      const uint32_t r = (uint32_t)(i / STAGES);
+      int ok = 1;
+      if (lane == 0)
+        ok = mbar_wait_bounded(bar_empty + 8 * s, (r & 1u) ^ 1u, abort_flag, args.status);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const uint32_t full = bar_full + 8 * s;
+      const int kk = (kbeg + i) * kBK;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(full, Cfg::STAGE_BYTES);
+        const uint32_t a_dst = sA + s * Cfg::A_BYTES;
+        tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
+        if (two_a) tma_load_2d(a_dst + a_half_bytes, tma_a, full, kk, a_row1, pol_w);
+        if (!gather) tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, pos0, pol_x);
+      }
+      if (gather) {
+#pragma unroll
+        for (int gq = 0; gq < 2; ++gq) {
+          const int grp4 = lane + 32 * gq;
+          if (grp4 * 4 < BN)
+            tma_gather4(sB + s * Cfg::B_BYTES + grp4 * 4 * 128, tma_b, full, kk % args.K,
+                        grow[gq][0], grow[gq][1], grow[gq][2], grow[gq][3], pol_x);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
+      const uint32_t idesc = idesc_bf16_f32(128, n_mma);
       for (int i = 0; i < nk; ++i) {
         const int s = i % STAGES;
         const uint32_t r = (uint32_t)(i / STAGES);
         if (!mbar_wait_bounded(bar_full + 8 * s, r & 1u, abort_flag, args.status)) break;
         tc_fence_after();
-        const uint32_t a_base = sA + s * kATileBytes;
+        const uint32_t a_base = sA + s * Cfg::A_BYTES;
         const uint32_t b_base = sB + s * Cfg::B_BYTES;
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
           // advance 16 bf16 (32 B) along K inside the 128-byte swizzle span
-          tc_mma_bf16(tmem, sw128_desc(a_base + 32 * k), sw128_desc(b_base + 32 * k), idesc,
-                      (i | k) != 0);
+          const uint64_t bdesc = sw128_desc(b_base + 32 * k);
+#pragma unroll
+          for (int t = 0; t < MT; ++t)
+            tc_mma_bf16(tmem + t * BN, sw128_desc(a_base + t * kATileBytes + 32 * k), bdesc,
+                        idesc, (i | k) != 0);
         }
         tc_commit(bar_empty + 8 * s);
       }
@@ -198,77 +348,100 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok) {
       float* S = reinterpret_cast<float*>(smem);  // [BN][128] fp32, token-major
       const int m = q4 * 32 + lane;
+      const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+      const bool exact = G.flags & FUS_GEMM_SWIGLU_EXACT;
+      // passes: SwiGLU with MT=2 pairs both accumulators in one pass; otherwise one pass
+      // per accumulator (128 output features each)
+      constexpr int PASSES = (EPI == FUS_EPI_SWIGLU) ? 1 : MT;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c, v);
+      for (int pass = 0; pass < PASSES; ++pass) {
+#pragma unroll 1
+        for (int c = 0; c < n_mma; c += 16) {
+          float v[16];
+          if (EPI == FUS_EPI_SWIGLU && MT == 2) {
+            float w[16];
+            tmem_ld16(lane_base + (uint32_t)c, v);         // gate feature m
+            tmem_ld16(lane_base + (uint32_t)(BN + c), w);  // up feature m
 #pragma unroll
-        for (int j = 0; j < 16; ++j) S[(c + j) * 128 + m] = v[j];
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-
-      const int pos0 = blk * BN;
-      if (EPI == FUS_EPI_SWIGLU) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(G.out);
-        for (int it = et; it < BN * 8; it += 128) {
-          const int j = it >> 3, q = it & 7;
-          const int pos = pos0 + j;
-          const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
-          if (row >= G.row_limit) continue;
-          const float4* gp = reinterpret_cast<const float4*>(S + j * 128 + q * 8);
-          const float4* up = reinterpret_cast<const float4*>(S + j * 128 + 64 + q * 8);
-          float g[8], u[8], o[8];
-          *reinterpret_cast<float4*>(g) = gp[0];
-          *reinterpret_cast<float4*>(g + 4) = gp[1];
-          *reinterpret_cast<float4*>(u) = up[0];
-          *reinterpret_cast<float4*>(u + 4) = up[1];
-          if (!(G.flags & FUS_GEMM_SWIGLU_EXACT)) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              g[e] = round_bf(g[e]);
-              u[e] = round_bf(u[e]);
+            for (int j = 0; j < 16; ++j) {
+              const float g = exact ? v[j] : round_bf(v[j]);
+              const float up = exact ? w[j] : round_bf(w[j]);
+              v[j] = (g / (1.0f + expf(-g))) * up;
             }
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + expf(-g[e]))) * u[e];
-          *reinterpret_cast<uint4*>(out + (long)row * G.ldo + mt * 64 + q * 8) = pack8(o);
-        }
-      } else if (EPI == FUS_EPI_BF16) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(G.out);
-        for (int it = et; it < BN * 16; it += 128) {
-          const int j = it >> 4, q = it & 15;
-          const int pos = pos0 + j;
-          const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
-          if (row >= G.row_limit) continue;
-          const float sc = G.row_scale ? __ldg(G.row_scale + row) : 1.0f;
-          const float4* sp = reinterpret_cast<const float4*>(S + j * 128 + q * 8);
-          float v[8];
-          *reinterpret_cast<float4*>(v) = sp[0];
-          *reinterpret_cast<float4*>(v + 4) = sp[1];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] *= sc;
-          if (G.flags & FUS_GEMM_OUT_F32) {
-            float4* dp = reinterpret_cast<float4*>(reinterpret_cast<float*>(G.out) +
-                                                   (long)row * G.ldo + mt * 128 + q * 8);
-            dp[0] = make_float4(v[0], v[1], v[2], v[3]);
-            dp[1] = make_float4(v[4], v[5], v[6], v[7]);
           } else {
-            *reinterpret_cast<uint4*>(out + (long)row * G.ldo + mt * 128 + q * 8) = pack8(v);
+            tmem_ld16(lane_base + (uint32_t)(pass * BN + c), v);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) S[(c + j) * 128 + m] = v[j];
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+
+        if (EPI == FUS_EPI_SWIGLU && MT == 1) {
+          // rows 0-63 of the tile are gate features, 64-127 the matching up features
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(G.out);
+          for (int it = et; it < n_live * 8; it += 128) {
+            const int j = it >> 3, q = it & 7;
+            const int pos = pos0 + j;
+            const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
+            if (row >= G.row_limit) continue;
+            const float4* gp = reinterpret_cast<const float4*>(S + j * 128 + q * 8);
+            const float4* up = reinterpret_cast<const float4*>(S + j * 128 + 64 + q * 8);
+            float g[8], uu[8], o[8];
+            *reinterpret_cast<float4*>(g) = gp[0];
+            *reinterpret_cast<float4*>(g + 4) = gp[1];
+            *reinterpret_cast<float4*>(uu) = up[0];
+            *reinterpret_cast<float4*>(uu + 4) = up[1];
+            if (!exact) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                g[e] = round_bf(g[e]);
+                uu[e] = round_bf(uu[e]);
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + expf(-g[e]))) * uu[e];
+            *reinterpret_cast<uint4*>(out + (long)row * G.ldo + mt * 64 + q * 8) = pack8(o);
+          }
+        } else {
+          // 128 finished features per token row: SwiGLU (MT=2) output, or one accumulator
+          const int col0 = (EPI == FUS_EPI_SWIGLU) ? mt * 128 : (mt * MT + pass) * 128;
+          for (int it = et; it < n_live * 16; it += 128) {
+            const int j = it >> 4, q = it & 15;
+            const int pos = pos0 + j;
+            const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
+            if (row >= G.row_limit) continue;
+            const float4* sp = reinterpret_cast<const float4*>(S + j * 128 + q * 8);
+            float vv[8];
+            *reinterpret_cast<float4*>(vv) = sp[0];
+            *reinterpret_cast<float4*>(vv + 4) = sp[1];
+            if (EPI == FUS_EPI_F32) {
+              float* dp = reinterpret_cast<float*>(G.out) + (long)split * args.split_stride +
+                          (long)row * G.ldo + col0 + q * 8;
+              reinterpret_cast<float4*>(dp)[0] = sp[0];
+              reinterpret_cast<float4*>(dp)[1] = sp[1];
+              continue;
+            }
+            if (EPI == FUS_EPI_BF16) {
+              const float sc = G.row_scale ? __ldg(G.row_scale + row) : 1.0f;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) vv[e] *= sc;
+              if (G.flags & FUS_GEMM_OUT_F32) {
+                float4* dp = reinterpret_cast<float4*>(reinterpret_cast<float*>(G.out) +
+                                                       (long)row * G.ldo + col0 + q * 8);
+                dp[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+                dp[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+                continue;
+              }
+            }
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(G.out) +
+                                      (long)row * G.ldo + col0 + q * 8) = pack8(vv);
           }
         }
-      } else {
-        float* out = reinterpret_cast<float*>(G.out) + (long)split * args.split_stride;
-        for (int it = et; it < BN * 16; it += 128) {
-          const int j = it >> 4, q = it & 15;
-          const int pos = pos0 + j;
-          const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
-          if (row >= G.row_limit) continue;
-          const float4* sp = reinterpret_cast<const float4*>(S + j * 128 + q * 8);
-          float4* dp = reinterpret_cast<float4*>(out + (long)row * G.ldo + mt * 128 + q * 8);
-          dp[0] = sp[0];
-          dp[1] = sp[1];
-        }
+        if (pass + 1 < PASSES) asm volatile("bar.sync 1, 128;" ::: "memory");
       }
+      if (EPI == FUS_EPI_BF16 && (G.flags & FUS_GEMM_MERGE) && args.mg.counters)
+        fused_merge_tail<BN, MT>(args, G, smem + Cfg::RING_BYTES - BN * 4 - 16, pos0, n_live, mt,
+                                 et);
     }
   }
 
@@ -287,30 +460,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ======================================================================================
 namespace {
 
-template <int BN, int EPI>
+template <int BN, int EPI, int MT>
 int launch_t(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t st) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, MT>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI>,
+    attr_err = cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, MT>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
                                                 cudaGetErrorString(attr_err));
-  grouped_gemm_kernel<BN, EPI><<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(maps[0], maps[1], maps[2],
-                                                                       maps[3], a);
+  grouped_gemm_kernel<BN, EPI, MT><<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(
+      maps[0], maps[1], maps[2], maps[3], a);
   return check_launch("grouped_gemm");
 }
 
 template <int EPI>
-int launch_bn(int bn, const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t st) {
-  switch (bn) {
-    case 16: return launch_t<16, EPI>(maps, a, grid, st);
-    case 32: return launch_t<32, EPI>(maps, a, grid, st);
-    case 64: return launch_t<64, EPI>(maps, a, grid, st);
-    case 128: return launch_t<128, EPI>(maps, a, grid, st);
-    case 256: return launch_t<256, EPI>(maps, a, grid, st);
+int launch_bn(int bn, int mt2, const CUtensorMap* maps, const GemmArgs& a, int grid,
+              cudaStream_t st) {
+  if (mt2) {
+    switch (bn) {
+      case 64: return launch_t<64, EPI, 2>(maps, a, grid, st);
+      case 128: return launch_t<128, EPI, 2>(maps, a, grid, st);
+      case 256: return launch_t<256, EPI, 2>(maps, a, grid, st);
+    }
+  } else {
+    switch (bn) {
+      case 16: return launch_t<16, EPI, 1>(maps, a, grid, st);
+      case 32: return launch_t<32, EPI, 1>(maps, a, grid, st);
+      case 64: return launch_t<64, EPI, 1>(maps, a, grid, st);
+      case 128: return launch_t<128, EPI, 1>(maps, a, grid, st);
+      case 256: return launch_t<256, EPI, 1>(maps, a, grid, st);
+    }
   }
   return set_error(FUS_E_UNSUPPORTED, "block_n %d not in {16,32,64,128,256}", bn);
 }
@@ -320,9 +502,59 @@ int launch_bn(int bn, const CUtensorMap* maps, const GemmArgs& a, int grid, cuda
 
 using namespace fus;
 
+static int mt2_for(int w_rows, int epilogue, int block_n) {
+  // two weight tiles per CTA for wide token tiles (prefill); the router (fp32 partials,
+  // split-K) keeps one for parallelism
+  return block_n >= 64 && epilogue != FUS_EPI_F32 && w_rows % 256 == 0;
+}
+
+static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
+                             int a_kplanes, int epilogue, int block_n, int ksplit,
+                             long split_stride, int group_blocks, const fus_merge_spec* merge,
+                             void* stream, int* status);
+
 extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
                                 int a_kplanes, int epilogue, int block_n, int ksplit,
                                 long split_stride, void* stream, int* status) {
+  return grouped_gemm_impl(groups, ngroups, w_rows, K, a_kplanes, epilogue, block_n, ksplit,
+                           split_stride, 0, nullptr, stream, status);
+}
+
+extern "C" int fus_grouped_gemm_ex(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
+                                   int a_kplanes, int epilogue, int block_n, int ksplit,
+                                   long split_stride, int group_blocks, void* stream,
+                                   int* status) {
+  return grouped_gemm_impl(groups, ngroups, w_rows, K, a_kplanes, epilogue, block_n, ksplit,
+                           split_stride, group_blocks, nullptr, stream, status);
+}
+
+extern "C" int fus_grouped_gemm_tiles(int w_rows, int epilogue, int block_n) {
+  if (w_rows <= 0 || w_rows % 128) return 0;
+  const int MTv = mt2_for(w_rows, epilogue, block_n) ? 2 : 1;
+  return epilogue == FUS_EPI_SWIGLU ? w_rows / 2 / (64 * MTv) : w_rows / (128 * MTv);
+}
+
+extern "C" int fus_grouped_gemm_merge(const fus_gemm_group* groups, int ngroups, int w_rows,
+                                      int K, int block_n, const fus_merge_spec* merge,
+                                      void* stream, int* status) {
+  if (!merge || !merge->counters || !merge->y || !merge->w || !merge->out || merge->parts < 1 ||
+      merge->topk < 1)
+    return set_error(FUS_E_INVALID, "grouped_gemm_merge: incomplete merge spec");
+  if (!aligned16(merge->y) || !aligned16(merge->out) || (merge->res && !aligned16(merge->res)) ||
+      (merge->extra && !aligned16(merge->extra)) || merge->ld_t % 8 || merge->ld_k % 8 ||
+      merge->ldo % 8 || merge->ldr % 8 || merge->lde % 4)
+    return set_error(FUS_E_INVALID, "grouped_gemm_merge: rows must be 16-byte aligned");
+  for (int g = 0; g < ngroups; ++g)
+    if ((groups[g].flags & FUS_GEMM_MERGE) && groups[g].token_div < 1)
+      return set_error(FUS_E_INVALID, "grouped_gemm_merge: token_div must be >= 1");
+  return grouped_gemm_impl(groups, ngroups, w_rows, K, 1, FUS_EPI_BF16, block_n, 1, 0, 0, merge,
+                           stream, status);
+}
+
+static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
+                             int a_kplanes, int epilogue, int block_n, int ksplit,
+                             long split_stride, int group_blocks, const fus_merge_spec* merge,
+                             void* stream, int* status) {
   if (!groups || ngroups < 1 || ngroups > 2)
     return set_error(FUS_E_INVALID, "ngroups must be 1 or 2");
   if (K <= 0 || K % kBK) return set_error(FUS_E_INVALID, "K=%d must be a positive multiple of 64", K);
@@ -334,6 +566,10 @@ extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w
   if (ksplit < 1) return set_error(FUS_E_INVALID, "ksplit must be >= 1");
   if (ksplit > 1 && epilogue != FUS_EPI_F32)
     return set_error(FUS_E_INVALID, "split-K needs the fp32 partial epilogue");
+  if (group_blocks < 0) return set_error(FUS_E_INVALID, "group_blocks < 0");
+
+  const int mt2 = mt2_for(w_rows, epilogue, block_n);
+  const int MTv = mt2 ? 2 : 1;
 
   GemmArgs a{};
   a.w_rows = w_rows;
@@ -341,13 +577,39 @@ extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w
   a.ksteps_total = a_kplanes * K / kBK;
   a.ksteps_per_split = (a.ksteps_total + ksplit - 1) / ksplit;
   a.ksplit = (a.ksteps_total + a.ksteps_per_split - 1) / a.ksteps_per_split;
-  a.m_tiles = w_rows / 128;
+  a.m_tiles = w_rows / (128 * MTv);
   a.split_stride = split_stride;
   a.status = status;
+  if (merge) {
+    a.mg.counters = merge->counters;
+    a.mg.parts = merge->parts;
+    a.mg.y = reinterpret_cast<const __nv_bfloat16*>(merge->y);
+    a.mg.ld_t = merge->ld_t;
+    a.mg.ld_k = merge->ld_k;
+    a.mg.topk = merge->topk;
+    a.mg.w = merge->w;
+    a.mg.ldw = merge->ldw;
+    a.mg.res = reinterpret_cast<const __nv_bfloat16*>(merge->res);
+    a.mg.ldr = merge->ldr;
+    a.mg.extra = merge->extra;
+    a.mg.lde = merge->lde;
+    a.mg.out = reinterpret_cast<__nv_bfloat16*>(merge->out);
+    a.mg.ldo = merge->ldo;
+  }
+  if (group_blocks == 0) {
+    // several blocks per expert (or a multi-block dense group): sweep 8 blocks together
+    long blocks = 0, experts = 0;
+    for (int g = 0; g < ngroups; ++g) {
+      blocks += groups[g].max_blocks;
+      experts += groups[g].n_experts;
+    }
+    group_blocks = blocks > 2 * experts ? 8 : 1;
+  }
+  a.group_blocks = group_blocks;
 
   CUtensorMap maps[4];
   long units[2] = {0, 0};
-  const int a_box_rows = epilogue == FUS_EPI_SWIGLU ? 64 : 128;
+  const int a_box_rows = (epilogue == FUS_EPI_SWIGLU && !mt2) ? 64 : 128;
   const int out_cols = epilogue == FUS_EPI_SWIGLU ? w_rows / 2 : w_rows;
   for (int g = 0; g < ngroups; ++g) {
     const fus_gemm_group& G = groups[g];
@@ -364,8 +626,10 @@ extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w
                                (uint64_t)G.n_experts * w_rows, (uint64_t)a_kplanes * K, kBK,
                                a_box_rows);
     if (rc) return rc;
+    if (G.gather_ids && !G.live_ids)
+      return set_error(FUS_E_INVALID, "group %d: gathered rows need live_ids/live_limit", g);
     rc = make_tmap_bf16_2d(&maps[2 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows, (uint64_t)G.ldx,
-                           kBK, block_n);
+                           kBK, G.gather_ids ? 1 : block_n);
     if (rc) return rc;
     GroupDev& D = a.g[g];
     D.expert_ids = G.expert_ids;
@@ -379,6 +643,11 @@ extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w
     D.row_map = G.row_map;
     D.row_scale = G.row_scale;
     D.flags = G.flags;
+    D.live_ids = G.live_ids;
+    D.live_limit = G.live_limit;
+    D.token_div = G.token_div > 0 ? G.token_div : 1;
+    D.gather_ids = G.gather_ids;
+    D.gather_div = G.gather_div > 0 ? G.gather_div : 1;
     units[g] = (long)G.max_blocks * a.m_tiles * a.ksplit;
   }
   if (ngroups == 1) {
@@ -391,8 +660,8 @@ extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w
   a.units0 = (int)units[0];
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (epilogue) {
-    case FUS_EPI_BF16: return launch_bn<FUS_EPI_BF16>(block_n, maps, a, (int)total, st);
-    case FUS_EPI_SWIGLU: return launch_bn<FUS_EPI_SWIGLU>(block_n, maps, a, (int)total, st);
-    default: return launch_bn<FUS_EPI_F32>(block_n, maps, a, (int)total, st);
+    case FUS_EPI_BF16: return launch_bn<FUS_EPI_BF16>(block_n, mt2, maps, a, (int)total, st);
+    case FUS_EPI_SWIGLU: return launch_bn<FUS_EPI_SWIGLU>(block_n, mt2, maps, a, (int)total, st);
+    default: return launch_bn<FUS_EPI_F32>(block_n, mt2, maps, a, (int)total, st);
   }
 }

@@ -138,6 +138,74 @@ __global__ void __launch_bounds__(kTopkWarps * 32)
   }
 }
 
+// CUDA-core fp32 GEMV for small T: CTA = 2 experts x all tokens. Every weight element is
+// reassembled exactly from its bf16 planes (hi + mid + lo, each sum exact) and used in
+// fp32 FMAs, so the result is an fp32 dot product like the reference's F.linear.
+constexpr int kGemvThreads = 256;
+constexpr int kGemvExperts = 2;
+constexpr int kGemvTokens = 8;
+constexpr int kGemvMaxT = 16;
+
+template <int NP>
+__global__ void __launch_bounds__(kGemvThreads)
+    router_gemv_kernel(const __nv_bfloat16* __restrict__ x2, long ldx,
+                       const __nv_bfloat16* __restrict__ wa, float* __restrict__ logits, int T,
+                       int H, int E) {
+  __shared__ float red[kGemvThreads / 32][kGemvExperts * kGemvTokens];
+  const int e0 = blockIdx.x * kGemvExperts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunk = H >> 3;
+  for (int t0 = 0; t0 < T; t0 += kGemvTokens) {
+    float acc[kGemvExperts][kGemvTokens];
+#pragma unroll
+    for (int a = 0; a < kGemvExperts; ++a)
+#pragma unroll
+      for (int b = 0; b < kGemvTokens; ++b) acc[a][b] = 0.f;
+    for (int c = threadIdx.x; c < nchunk; c += kGemvThreads) {
+      float w[kGemvExperts][8];
+#pragma unroll
+      for (int a = 0; a < kGemvExperts; ++a) {
+        const __nv_bfloat16* row = wa + (long)(e0 + a) * NP * H + c * 8;
+        unpack8(__ldg(reinterpret_cast<const uint4*>(row)), w[a]);
+#pragma unroll
+        for (int p = 1; p < NP; ++p) {
+          float q[8];
+          unpack8(__ldg(reinterpret_cast<const uint4*>(row + (long)p * H)), q);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[a][i] += q[i];
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kGemvTokens; ++b) {
+        if (t0 + b < T) {
+          float x[8];
+          unpack8(__ldg(reinterpret_cast<const uint4*>(x2 + (long)(t0 + b) * ldx + c * 8)), x);
+#pragma unroll
+          for (int a = 0; a < kGemvExperts; ++a)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[a][b] = fmaf(x[i], w[a][i], acc[a][b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < kGemvExperts; ++a)
+#pragma unroll
+      for (int b = 0; b < kGemvTokens; ++b) {
+        const float v = warp_sum(acc[a][b]);
+        if (lane == 0) red[warp][a * kGemvTokens + b] = v;
+      }
+    __syncthreads();
+    if (threadIdx.x < kGemvExperts * kGemvTokens) {
+      const int a = threadIdx.x / kGemvTokens, b = threadIdx.x % kGemvTokens;
+      float v = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kGemvThreads / 32; ++w2) v += red[w2][threadIdx.x];
+      if (t0 + b < T) logits[(long)(t0 + b) * E + e0 + a] = v;
+    }
+    __syncthreads();
+  }
+}
+
 int router_block_n(int T) {
   return T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
 }
@@ -164,6 +232,7 @@ extern "C" int fus_router_transpose_weight(const void* wgt, void* wa, int H, int
 
 extern "C" int fus_router_nsplit(int T, int H, int E, int nplanes) {
   if (T <= 0 || H <= 0 || E <= 0 || nplanes <= 0 || H % 64 || E % 128) return 1;
+  if (T <= kGemvMaxT) return 1;  // CUDA-core GEMV path writes the logits directly
   const int bn = router_block_n(T);
   const long units = (long)(E / 128) * ceil_div(T, bn);
   const int ksteps = nplanes * H / 64;
@@ -183,6 +252,19 @@ extern "C" int fus_router_logits(const void* x2, long ldx, const void* wa, int n
   if (E % 128) return set_error(FUS_E_UNSUPPORTED, "router_logits: E=%d must be a multiple of 128", E);
   if (H % 64) return set_error(FUS_E_UNSUPPORTED, "router_logits: H=%d must be a multiple of 64", H);
   if (T == 0) return FUS_OK;
+  if (T <= kGemvMaxT && (nplanes == 1 || nplanes == 3)) {
+    if (nsplit != 1) return set_error(FUS_E_INVALID, "router_logits: nsplit must be 1 for T <= 16");
+    if (!aligned16(x2) || ldx % 8 || !aligned16(wa))
+      return set_error(FUS_E_INVALID, "router_logits: rows must be 16-byte aligned");
+    const int grid = E / kGemvExperts;
+    if (nplanes == 3)
+      router_gemv_kernel<3><<<grid, kGemvThreads, 0, as_stream(stream)>>>(
+          (const __nv_bfloat16*)x2, ldx, (const __nv_bfloat16*)wa, partial, T, H, E);
+    else
+      router_gemv_kernel<1><<<grid, kGemvThreads, 0, as_stream(stream)>>>(
+          (const __nv_bfloat16*)x2, ldx, (const __nv_bfloat16*)wa, partial, T, H, E);
+    return check_launch("router_gemv");
+  }
   const int ksteps = nplanes * H / 64;
   if (nsplit < 1 || nsplit > ksteps || ceil_div(ksteps, ceil_div(ksteps, nsplit)) != nsplit)
     return set_error(FUS_E_INVALID, "router_logits: nsplit=%d not normalised (use fus_router_nsplit)",

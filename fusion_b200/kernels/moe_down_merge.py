@@ -25,7 +25,8 @@ def _down_rows(a, w2, y, topk_weights_flat, sti, eid, ntp, num_valid_tokens, bm)
     a_rows = _ws.scratch("down_rows", EM * K, torch.bfloat16, a.device).view(EM, K)
     ops.permute_rows(a, sti, ntp, 1, num_valid_tokens, a_rows, EM)
     g = ops.gemm_group(w2, a_rows, y, expert_ids=eid, ntp=ntp, max_blocks=EM // bm, row_map=sti,
-                       row_limit=num_valid_tokens, row_scale=topk_weights_flat)
+                       row_limit=num_valid_tokens, row_scale=topk_weights_flat,
+                       live_ids=sti, live_limit=num_valid_tokens)
     ops.grouped_gemm([g], w2.shape[-2], K, ops.FUS_EPI_BF16, bm)
 
 

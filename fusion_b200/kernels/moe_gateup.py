@@ -38,7 +38,8 @@ def launch_gateup(a, w13, c, sorted_token_ids, expert_ids, num_tokens_post_padde
     g = ops.gemm_group(w13, xs, c, expert_ids=expert_ids, ntp=num_tokens_post_padded,
                        max_blocks=EM // bm, row_map=sorted_token_ids,
                        row_limit=num_valid_tokens,
-                       flags=ops.GEMM_SWIGLU_EXACT if fused else 0)
+                       flags=ops.GEMM_SWIGLU_EXACT if fused else 0,
+                       live_ids=sorted_token_ids, live_limit=num_valid_tokens)
     ops.grouped_gemm([g], w13.shape[-2], H, ops.FUS_EPI_SWIGLU if fused else ops.FUS_EPI_BF16, bm)
 
 

@@ -14,7 +14,7 @@ import torch
 from . import _lib as L
 
 FUS_EPI_BF16, FUS_EPI_SWIGLU, FUS_EPI_F32 = 0, 1, 2
-GEMM_OUT_F32, GEMM_SWIGLU_EXACT = 0x1, 0x2
+GEMM_OUT_F32, GEMM_SWIGLU_EXACT, GEMM_W_STREAM, GEMM_MERGE = 0x1, 0x2, 0x4, 0x8
 ERR_TIMEOUT, ERR_BAD_EXPERT, ERR_CAPACITY = 0x1, 0x2, 0x4
 
 _status: dict[int, torch.Tensor] = {}
@@ -123,6 +123,19 @@ def moe_align(ids, E: int, block_m: int, sorted_ids, expert_ids, ntp, workspace=
            need, _stream(), _sp())
 
 
+def route_small(h, r, gamma, wa, nplanes: int, bias, h1, x2, logits, topw, topi, block_m: int,
+                sorted_ids, expert_ids, ntp, done, zero=None, eps: float = 1e-5,
+                scale: float = 2.5, renorm: bool = True):
+    """Decode front end (T <= 16): norm + router + top-k + layout in one launch."""
+    T, H = h.shape
+    E = logits.shape[1]
+    topk = topi.shape[1]
+    L.call("fus_moe_route_small", _p(h), _p(r), _p(gamma), eps, _p(wa), nplanes, _p(bias), T, H, E,
+           topk, scale, int(renorm), _p(h1), _p(x2), _p(logits), _p(topw), _p(topi), block_m,
+           _p(sorted_ids), sorted_ids.numel(), _p(expert_ids), expert_ids.numel(), _p(ntp),
+           _p(done), _p(zero), zero.numel() if zero is not None else 0, _stream(), _sp())
+
+
 def permute_rows(src, sorted_ids, ntp, div: int, num_valid: int, dst, max_rows: int | None = None):
     H = src.shape[1]
     if max_rows is None:
@@ -133,7 +146,8 @@ def permute_rows(src, sorted_ids, ntp, div: int, num_valid: int, dst, max_rows: 
 
 def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map=None,
                row_limit: int, row_scale=None, x_rows: int | None = None,
-               flags: int = 0) -> L.GemmGroup:
+               flags: int = 0, live_ids=None, live_limit: int = 0,
+               token_div: int = 1, gather_ids=None, gather_div: int = 1) -> L.GemmGroup:
     """Describe one weight stack + token rows for :func:`grouped_gemm`.
 
     ``w`` is [n_experts, w_rows, K'] (or [w_rows, K'] for one expert) bf16."""
@@ -152,14 +166,48 @@ def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map
     g.row_limit = row_limit
     g.row_scale = _p(row_scale)
     g.flags = flags
+    g.live_ids = _p(live_ids)
+    g.live_limit = live_limit
+    g.token_div = token_div
+    g.gather_ids = _p(gather_ids)
+    g.gather_div = gather_div
     return g
 
 
 def grouped_gemm(groups: list[L.GemmGroup], w_rows: int, K: int, epilogue: int, block_n: int,
-                 a_kplanes: int = 1, ksplit: int = 1, split_stride: int = 0):
+                 a_kplanes: int = 1, ksplit: int = 1, split_stride: int = 0,
+                 group_blocks: int = 0):
     arr = (L.GemmGroup * len(groups))(*groups)
-    L.call("fus_grouped_gemm", arr, len(groups), w_rows, K, a_kplanes, epilogue, block_n, ksplit,
-           split_stride, _stream(), _sp())
+    L.call("fus_grouped_gemm_ex", arr, len(groups), w_rows, K, a_kplanes, epilogue, block_n,
+           ksplit, split_stride, group_blocks, _stream(), _sp())
+
+
+def gemm_tiles(w_rows: int, epilogue: int, block_n: int) -> int:
+    return int(L.lib().fus_grouped_gemm_tiles(w_rows, epilogue, block_n))
+
+
+def grouped_gemm_merge(groups: list[L.GemmGroup], w_rows: int, K: int, block_n: int, *,
+                       counters, y3, w, res, extra, out, parts: int):
+    """Down projection with the expert merge fused into its epilogue.
+    y3: [T, topk, H] bf16 rows the routed group writes; counters: zeroed int32
+    [T * gemm_tiles(w_rows, FUS_EPI_BF16, block_n)] (left zero afterwards)."""
+    m = L.MergeSpec()
+    m.counters = _p(counters)
+    m.parts = parts
+    m.y = _p(y3)
+    m.ld_t, m.ld_k = y3.stride(0), y3.stride(1)
+    m.topk = y3.shape[1]
+    m.w = _p(w)
+    m.ldw = w.stride(0)
+    m.res = _p(res)
+    m.ldr = _ld(res) if res is not None else 0
+    m.extra = _p(extra)
+    m.lde = _ld(extra) if extra is not None else 0
+    m.out = _p(out)
+    m.ldo = _ld(out)
+    arr = (L.GemmGroup * len(groups))(*groups)
+    L.call("fus_grouped_gemm_merge", arr, len(groups), w_rows, K, block_n, C.byref(m), _stream(),
+           _sp())
 
 
 def silu_and_mul(x, y):

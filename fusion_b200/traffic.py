@@ -65,7 +65,7 @@ def block_kernels(T: int, ne: float, H: int = 6144, I: int = 2048, E: int = 256,
     return [
         KernelCost("add_rmsnorm", 0.0, 4 * act + H * BF16),
         KernelCost("router", 2.0 * T * H * E, act + E * H * FP32 + T * E * FP32 + T * topk * 8),
-        KernelCost("align_permute", 0.0, T * topk * I32 * 3 + R * H * BF16),
+        KernelCost("align", 0.0, T * topk * I32 * 3),
         KernelCost("w13_swiglu", 2.0 * (R + ns * T) * H * 2 * I,
                    (ne + ns) * w13_e + (R + ns * T) * H * BF16 + (R + ns * T) * I * BF16),
         KernelCost("w2", 2.0 * (R + ns * T) * I * H,

@@ -50,6 +50,10 @@ extern "C" {
 #define FUS_GEMM_OUT_F32 0x1      /* FUS_EPI_BF16 writes fp32 instead of bf16                */
 #define FUS_GEMM_SWIGLU_EXACT 0x2 /* SwiGLU on fp32 gate/up; default rounds them to bf16     */
                                   /* first, as the framework's unfused chain does          */
+#define FUS_GEMM_W_STREAM 0x4     /* each weight tile is read by one token block only:      */
+                                  /* load it L2 evict-first (decode); default evict-normal */
+#define FUS_GEMM_MERGE 0x8        /* this group's rows take part in the fused merge of     */
+                                  /* fus_grouped_gemm_merge (token = row / token_div)      */
 
 int fus_version(void);
 const char* fus_last_error(void);
@@ -81,7 +85,9 @@ int fus_router_transpose_weight(const void* wgt, void* wa, int H, int E, void* s
 /* Router GEMM (glm52/kernels/norm_router.py:347 router_gemm; reference.py:61):
  * partial[s, t, e] = sum over the s-th K split of x2[t,:] . wa[e, :] (fp32).
  * Summing the nsplit planes (fus_router_topk does, in fixed order) gives
- * logits = x2.float() @ W.float().T. Use fus_router_nsplit() for nsplit. */
+ * logits = x2.float() @ W.float().T. Use fus_router_nsplit() for nsplit. Up to
+ * T = 16 tokens it is a CUDA-core fp32 GEMV over the reassembled weight (nsplit 1);
+ * above, the tcgen05 grouped GEMM over the planes. */
 int fus_router_nsplit(int T, int H, int E, int nplanes);
 int fus_router_logits(const void* x2, long ldx, const void* wa, int nplanes, float* partial,
                       int T, int H, int E, int nsplit, void* stream, int* status);
@@ -125,10 +131,25 @@ int fus_moe_align_noalloc(const int* ids, int numel, int E, int block_m, int* so
                           int sorted_cap, int* expert_ids, int blocks_cap, int* ntp, void* stream,
                           int* status);
 
+/* Decode front end in one launch (T <= 16): add_rmsnorm + fp32 router + top-k + dispatch
+ * layout (replaces fus_add_rmsnorm + fus_router_logits + fus_router_topk +
+ * fus_moe_align for small T). Every CTA normalises the T rows into shared memory and
+ * computes the logits of two experts; the last CTA to finish selects the top-k and
+ * builds the layout. `done` is an int that must be zero before the first call (each
+ * call leaves it zero); `zero`/`zero_n` optionally names an int buffer the call clears
+ * (the fused merge's counters). Requires E <= 256, E % 2 == 0, T*topk <= 256. */
+int fus_moe_route_small(const void* h, const void* r, const void* gamma, float eps, const void* wa,
+                        int nplanes, const float* bias, int T, int H, int E, int topk,
+                        float scale, int renorm, void* h1, void* x2, float* logits, float* topw,
+                        int* topi, int block_m, int* sorted_ids, int sorted_cap, int* expert_ids,
+                        int blocks_cap, int* ntp, int* done, int* zero, int zero_n, void* stream,
+                        int* status);
+
 /* Row permutation into dispatch order (the A gather `offs_token // top_k` of
  * glm52/kernels/moe_gateup.py:96-99, done once up front so the GEMM reads dense rows):
- *   dst[p] = src[sorted_ids[p] / div]  if sorted_ids[p] < num_valid, else zeros,
- * for p < min(ntp[0], max_rows). H % 8 == 0, 16-byte aligned rows. */
+ *   dst[p] = src[sorted_ids[p] / div]  if sorted_ids[p] < num_valid,
+ * for p < min(ntp[0], max_rows); pad rows are left untouched (the GEMMs neither
+ * multiply nor write dispatch pads). H % 8 == 0, 16-byte aligned rows. */
 int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp, int div,
                      int num_valid, void* dst, long ld_dst, int max_rows, int H, void* stream,
                      int* status);
@@ -170,11 +191,55 @@ typedef struct fus_gemm_group {
   int row_limit;
   const float* row_scale; /* optional, FUS_EPI_BF16 only                                   */
   int flags;              /* FUS_GEMM_* bits                                               */
+  const int* live_ids;    /* optional: column j of block b is live iff                     */
+  int live_limit;         /*   live_ids[b*block_n + j] < live_limit; dead columns sit at   */
+                          /*   the end of a block (dispatch pads) and are neither          */
+                          /*   multiplied (the MMA N shrinks) nor written                  */
+  int token_div;          /* FUS_GEMM_MERGE: token of output row r is r / token_div        */
+  const int* gather_ids;  /* optional: token rows are gathered, not read densely: row j of */
+  int gather_div;         /*   block b is x[gather_ids[b*block_n+j] / gather_div] when that */
+                          /*   id is live (< live_limit), zeros otherwise (TMA gather4)     */
 } fus_gemm_group;
 
 int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w_rows, int K, int a_kplanes,
                      int epilogue, int block_n, int ksplit, long split_stride, void* stream,
                      int* status);
+/* Same, with `group_blocks` consecutive token blocks swept across all weight tiles before
+ * the next group of blocks starts (0 = pick from block counts): blocks of one expert then
+ * share each weight tile through L2 while their token rows stay resident. */
+int fus_grouped_gemm_ex(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
+                        int a_kplanes, int epilogue, int block_n, int ksplit, long split_stride,
+                        int group_blocks, void* stream, int* status);
+
+/* Down projection with the expert merge fused into its epilogue (replaces
+ * glm52/kernels/moe_down_merge.py:427 launch_down + :504 launch_moe_sum / the F10
+ * merge, reference.py:159-188). Groups flagged FUS_GEMM_MERGE write their rows as
+ * fus_grouped_gemm does (epilogue FUS_EPI_BF16; fp32 rows with FUS_GEMM_OUT_F32), then
+ * count, per (token, weight tile), how many of the `parts` contributions have landed.
+ * The CTA that lands the last one computes, in a fixed order (deterministic),
+ *   out[t, f] = bf16( sum_k w[t,k] * y[t,k,f] + res[t,f] + extra[t,f] )
+ * for that tile's features and resets the counter. `counters` ([T * tiles] ints, tiles
+ * = fus_grouped_gemm_tiles()) must be zero before the first call; every call leaves
+ * them zero. */
+typedef struct fus_merge_spec {
+  int* counters;
+  int parts;            /* contributions per token: topk (+1 with a shared expert)        */
+  const void* y;        /* bf16 routed rows, row (t, k) at y + t*ld_t + k*ld_k            */
+  long ld_t, ld_k;
+  int topk;
+  const float* w;       /* [T, topk] routing weights, row stride ldw                      */
+  long ldw;
+  const void* res;      /* bf16 [T, H] residual (h1) or NULL                              */
+  long ldr;
+  const float* extra;   /* fp32 [T, H] shared-expert output or NULL                       */
+  long lde;
+  void* out;            /* bf16 [T, H]                                                     */
+  long ldo;
+} fus_merge_spec;
+
+int fus_grouped_gemm_tiles(int w_rows, int epilogue, int block_n);
+int fus_grouped_gemm_merge(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
+                           int block_n, const fus_merge_spec* merge, void* stream, int* status);
 
 /* ---------------------------------------------------------------------------------
  * Element-wise / merge kernels
@@ -213,7 +278,9 @@ int fus_seed(void* o, long ldo, const void* src, long lds, int M, int N, int fro
  *   act     = silu(x2 W13_gate^T) * (x2 W13_up^T)     per routed expert + shared
  *   y       = act W2^T
  *   out     = bf16( sum_k w_k y_k + h1 + y_shared )   (fp32 sum; x2, act, y stored bf16)
- * block_n = 0 picks the token tile from T. The workspace holds every intermediate.
+ * block_n = 0 picks the token tile from T. The workspace holds every intermediate and
+ * two sets of counters; it must be all zero before its first use (every call leaves
+ * the counters zero again).
  * ------------------------------------------------------------------------------- */
 typedef struct fus_moe_block_desc {
   int H, I, E, topk;

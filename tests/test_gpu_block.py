@@ -145,3 +145,66 @@ def test_block_graph_replay_matches_eager(weights_404):
     finish()
     assert torch.equal(outs.out.view(torch.int16), eager.out.view(torch.int16))
     assert torch.equal(outs.topi, eager.topi)
+
+
+@pytest.mark.parametrize("T", [3, 16])
+def test_fused_merge_matches_merge_kernel_and_rearms(weights_404, T):
+    """The w2 epilogue's last-arriver merge equals the standalone merge kernel bit for
+    bit (same summation order) and leaves its counters at zero."""
+    from fusion_b200.chain import BlockChain
+
+    blk = make_block(weights_404)
+    ch = BlockChain(blk, T)
+    h, r = synth.make_inputs(900 + T, T, D, DEV)
+    for _ in range(2):  # second call exercises the re-armed counters
+        ch.run(h, r)
+    finish()
+    ref = torch.empty_like(ch.outs.out)
+    ops.merge(ch.y.view(T, D.topk, D.H), ch.outs.topw, ch.outs.h1, ch.ys, ref, round_mid=False)
+    finish()
+    assert torch.equal(ch.outs.out.view(torch.int16), ref.view(torch.int16))
+    assert int(ch.counters.abs().sum().item()) == 0
+    eager = blk(h, r)
+    finish()
+    assert torch.equal(eager.out.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("T", [1, 5, 16])
+def test_route_small_equals_separate_kernels(weights_404, T):
+    """The one-launch decode front end reproduces add_rmsnorm + router + top-k + layout."""
+    w = weights_404
+    blk = make_block(w)
+    h, r = synth.make_inputs(1200 + T, T, D, DEV)
+    bn, E, K = 16, D.E, D.topk
+    cap = (T * K + E * (bn - 1) + bn - 1) // bn * bn
+    h1a, x2a = torch.empty_like(h), torch.empty_like(h)
+    ops.add_rmsnorm(h, r, w["gamma"], h1a, x2a)
+    ns = ops.router_nsplit(T, D.H, E, blk.nplanes)
+    part = torch.empty(ns, T, E, device=DEV)
+    ops.router_logits(x2a, blk.wa, blk.nplanes, part, ns)
+    twa = torch.empty(T, K, device=DEV)
+    tia = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    lga = torch.empty(T, E, device=DEV)
+    ops.router_topk(part, ns, w["bias"], lga, twa, tia)
+    sa = torch.full((cap,), -1, dtype=torch.int32, device=DEV)
+    ea = torch.full((cap // bn,), -1, dtype=torch.int32, device=DEV)
+    na = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.moe_align(tia, E, bn, sa, ea, na)
+    h1b, x2b = torch.empty_like(h), torch.empty_like(h)
+    twb, tib, lgb = torch.empty_like(twa), torch.empty_like(tia), torch.empty_like(lga)
+    sb, eb = torch.full_like(sa, -1), torch.full_like(ea, -1)
+    nb = torch.zeros(1, dtype=torch.int32, device=DEV)
+    done = torch.zeros(4, dtype=torch.int32, device=DEV)
+    junk = torch.full((64,), 7, dtype=torch.int32, device=DEV)
+    for _ in range(2):  # the ticket re-arms
+        ops.route_small(h, r, w["gamma"], blk.wa, blk.nplanes, w["bias"], h1b, x2b, lgb, twb,
+                        tib, bn, sb, eb, nb, done, junk)
+    finish()
+    assert torch.equal(h1a.view(torch.int16), h1b.view(torch.int16))
+    assert torch.equal(x2a.view(torch.int16), x2b.view(torch.int16))
+    assert torch.equal(tia, tib)
+    np.testing.assert_allclose(twb.cpu().numpy(), twa.cpu().numpy(), rtol=1e-6, atol=1e-7)
+    n = int(na.item())
+    assert int(nb.item()) == n and torch.equal(sa[:n], sb[:n])
+    assert torch.equal(ea[: n // bn], eb[: n // bn])
+    assert int(done.sum().item()) == 0 and int(junk.abs().sum().item()) == 0

@@ -53,17 +53,18 @@ def test_swiglu_and_down_small(bn):
         return torch.nn.functional.silu(h[:, :I]) * h[:, I:]
 
     ref = ref_rows(xs, w13, eids.cpu(), bn, swiglu)
-    assert rel_err(act.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+    live = torch.from_numpy(s.cpu().numpy() < R)  # dispatch pads are neither read nor written
+    assert rel_err(act.float().cpu()[live].numpy(), ref.cpu()[live].numpy()) < 1e-2
 
     # down projection with routed-weight scale, scattered to flat rows
     scale = torch.rand(R, device=DEV)
     y = torch.full((R, H), float("nan"), dtype=torch.bfloat16, device=DEV)
     g2 = ops.gemm_group(w2, act, y, expert_ids=eids, ntp=ntp, max_blocks=cap // bn, row_map=s,
-                        row_limit=R, row_scale=scale)
+                        row_limit=R, row_scale=scale, live_ids=s, live_limit=R)
     ops.grouped_gemm([g2], H, I, ops.FUS_EPI_BF16, bn)
     finish()
     yref = torch.empty(R, H, device=DEV)
-    down = ref_rows(act, w2, eids.cpu(), bn, lambda a, w: a @ w.t())
+    down = ref_rows(act, w2, eids.cpu(), bn, lambda a, w: a @ w.t())  # pad rows: garbage, unused
     sc = s.cpu().numpy()
     valid = torch.from_numpy(np.nonzero(sc < R)[0]).to(DEV)
     yref[s[valid].long()] = down[valid] * scale[s[valid].long()][:, None]
@@ -95,7 +96,8 @@ def test_two_groups_real_dims():
         return torch.nn.functional.silu(h[:, :I]) * h[:, I:]
 
     ref = ref_rows(xs, w13, eids.cpu(), bn, swiglu)
-    assert rel_err(act.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+    live = torch.from_numpy(s.cpu().numpy() < R)
+    assert rel_err(act.float().cpu()[live].numpy(), ref.cpu()[live].numpy()) < 1e-2
     refs = swiglu(x.float(), w13s.float())
     assert rel_err(act_s.float().cpu().numpy(), refs.cpu().numpy()) < 1e-2
 
@@ -118,3 +120,27 @@ def test_f32_planes_splitk(T, ksplit):
     got = part.sum(0)
     ref = x.double() @ w.double().t()
     assert (got.double() - ref).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("bn", [16, 128])
+def test_gathered_rows_equal_permuted_rows(bn):
+    """B rows gathered by the GEMM itself (TMA gather4 by dispatch position) give the same
+    bits as the same GEMM over rows permuted beforehand."""
+    T, K, E, H, I = 70, 8, 8, 1024, 256
+    ids, s, eids, ntp, cap = layout(T, K, E, bn, 11 + bn)
+    R = T * K
+    x = (torch.randn(T, H, device=DEV)).to(torch.bfloat16)
+    w13 = (torch.randn(E, 2 * I, H, device=DEV) * 0.05).to(torch.bfloat16)
+    xs = torch.zeros(cap, H, dtype=torch.bfloat16, device=DEV)
+    ops.permute_rows(x, s, ntp, K, R, xs)
+    a1 = torch.zeros(cap, I, dtype=torch.bfloat16, device=DEV)
+    a2 = torch.zeros(cap, I, dtype=torch.bfloat16, device=DEV)
+    g1 = ops.gemm_group(w13, xs, a1, expert_ids=eids, ntp=ntp, max_blocks=cap // bn,
+                        row_limit=cap, live_ids=s, live_limit=R)
+    g2 = ops.gemm_group(w13, x, a2, expert_ids=eids, ntp=ntp, max_blocks=cap // bn,
+                        row_limit=cap, live_ids=s, live_limit=R, gather_ids=s, gather_div=K)
+    ops.grouped_gemm([g1], 2 * I, H, ops.FUS_EPI_SWIGLU, bn)
+    ops.grouped_gemm([g2], 2 * I, H, ops.FUS_EPI_SWIGLU, bn)
+    finish()
+    live = torch.from_numpy(s.cpu().numpy() < R).to(DEV)
+    assert torch.equal(a1[live].view(torch.int16), a2[live].view(torch.int16))

@@ -196,8 +196,9 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   g[1].ldo = I;
   g[1].row_limit = T;
   g[1].flags = FUS_GEMM_SWIGLU_EXACT | (T <= block_n ? FUS_GEMM_W_STREAM : 0);
-  if ((rc = fus_grouped_gemm(g, shared ? 2 : 1, 2 * I, H, 1, FUS_EPI_SWIGLU, block_n, 1, 0, stream,
-                             status)))
+  // decode: launched early (programmatic dependent launch) behind the front end
+  if ((rc = grouped_gemm_launch(g, shared ? 2 : 1, 2 * I, H, 1, FUS_EPI_SWIGLU, block_n, 1, 0, 0,
+                                nullptr, small ? 1 : 0, stream, status)))
     return rc;
   // ---- w2: routed rows to y[flat], shared rows to ys (fp32) ----
   g[0].w = d->w2;
@@ -246,5 +247,8 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   m.lde = H;
   m.out = out;
   m.ldo = H;
-  return fus_grouped_gemm_merge(g, shared ? 2 : 1, H, I, block_n, &m, stream, status);
+  // launched early; its weight tiles stream in while the w13 grid drains (expert ids
+  // come from the front end, which finished before w13 started)
+  return grouped_gemm_launch(g, shared ? 2 : 1, H, I, 1, FUS_EPI_BF16, block_n, 1, 0, 0, &m, 2,
+                             stream, status);
 }

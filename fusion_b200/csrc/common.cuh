@@ -37,6 +37,17 @@ FUS_DEVICE uint64_t globaltimer_ns() {
 constexpr uint64_t kWaitBudgetNs = 1000000000ull;
 
 // ------------------------------------------------------------------------------------
+// programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before its predecessor finishes; `pdl_wait` blocks until the
+// predecessor grid completed and its writes are visible, `pdl_allow_dependents` lets
+// the next kernel start launching. Both are no-ops without the launch attribute.
+// ------------------------------------------------------------------------------------
+FUS_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+FUS_DEVICE void pdl_allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------------------------------------
 // bf16 helpers
 // ------------------------------------------------------------------------------------
 FUS_DEVICE float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }

@@ -70,6 +70,7 @@ struct GemmArgs {
   long split_stride;     // FUS_EPI_F32 partial plane stride (elements)
   int* status;
   MergeDev mg;
+  int pdl;  // 0 none; 1 wait before any read; 2 prefetch weights, then wait
 };
 
 constexpr int kBK = 64;                  // K elements per stage (128 B rows, one swizzle span)
@@ -187,6 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int gsz = min(args.group_blocks, G.max_blocks - grp * args.group_blocks);
   const int mt = rem / gsz;
   const int blk = grp * args.group_blocks + rem % gsz;
+  if (args.pdl == 1) pdl_wait();  // the dispatch layout comes from the predecessor
+  pdl_allow_dependents();
   const int rows_used = G.ntp ? __ldg(G.ntp) : G.x_rows;
   if (blk * BN >= rows_used) return;  // uniform across the CTA: nothing allocated yet
   const int expert = G.expert_ids ? __ldg(G.expert_ids + blk) : 0;
@@ -288,23 +291,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         grow[gq][q] = row;
       }
-    for (int i = 0; i < nk; ++i) {
-      const int s = i % STAGES;
-      const uint32_t r = (uint32_t)(i / STAGES);
-      int ok = 1;
-      if (lane == 0)
-        ok = mbar_wait_bounded(bar_empty + 8 * s, (r & 1u) ^ 1u, abort_flag, args.status);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+    // weight tiles of stage s, k-step i (lane 0; also posts the stage's byte count)
+    auto load_a = [&](int s, int i) {
       const uint32_t full = bar_full + 8 * s;
       const int kk = (kbeg + i) * kBK;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(full, Cfg::STAGE_BYTES);
-        const uint32_t a_dst = sA + s * Cfg::A_BYTES;
-        tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
-        if (two_a) tma_load_2d(a_dst + a_half_bytes, tma_a, full, kk, a_row1, pol_w);
-        if (!gather) tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, pos0, pol_x);
-      }
+      mbar_arrive_expect_tx(full, Cfg::STAGE_BYTES);
+      const uint32_t a_dst = sA + s * Cfg::A_BYTES;
+      tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
+      if (two_a) tma_load_2d(a_dst + a_half_bytes, tma_a, full, kk, a_row1, pol_w);
+    };
+    // token rows of stage s, k-step i (whole warp)
+    auto load_b = [&](int s, int i) {
+      const uint32_t full = bar_full + 8 * s;
+      const int kk = (kbeg + i) * kBK;
       if (gather) {
 #pragma unroll
         for (int gq = 0; gq < 2; ++gq) {
@@ -313,7 +312,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_gather4(sB + s * Cfg::B_BYTES + grp4 * 4 * 128, tma_b, full, kk % args.K,
                         grow[gq][0], grow[gq][1], grow[gq][2], grow[gq][3], pol_x);
         }
+      } else if (lane == 0) {
+        tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, pos0, pol_x);
       }
+    };
+    // pdl == 2: the weight tiles of the first ring are requested while the predecessor
+    // (which produces the token rows) is still running; token rows follow its completion
+    int i0 = 0;
+    if (args.pdl == 2) {
+      i0 = min(nk, STAGES);
+      if (lane == 0) {
+        for (int i = 0; i < i0; ++i) load_a(i, i);
+        pdl_wait();
+      }
+      __syncwarp();
+      for (int i = 0; i < i0; ++i) load_b(i, i);
+    }
+    for (int i = i0; i < nk; ++i) {
+      const int s = i % STAGES;
+      const uint32_t r = (uint32_t)(i / STAGES);
+      int ok = 1;
+      if (lane == 0)
+        ok = mbar_wait_bounded(bar_empty + 8 * s, (r & 1u) ^ 1u, abort_flag, args.status);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (lane == 0) load_a(s, i);
+      load_b(s, i);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -471,8 +495,19 @@ int launch_t(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t 
   });
   if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
                                                 cudaGetErrorString(attr_err));
-  grouped_gemm_kernel<BN, EPI, MT><<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(
-      maps[0], maps[1], maps[2], maps[3], a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<BN, EPI, MT>, maps[0], maps[1],
+                                     maps[2], maps[3], a);
+  if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "grouped_gemm: %s", cudaGetErrorString(e));
   return check_launch("grouped_gemm");
 }
 
@@ -511,7 +546,17 @@ static int mt2_for(int w_rows, int epilogue, int block_n) {
 static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
                              int a_kplanes, int epilogue, int block_n, int ksplit,
                              long split_stride, int group_blocks, const fus_merge_spec* merge,
-                             void* stream, int* status);
+                             void* stream, int* status, int pdl = 0);
+
+namespace fus {
+int grouped_gemm_launch(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
+                        int a_kplanes, int epilogue, int block_n, int ksplit, long split_stride,
+                        int group_blocks, const fus_merge_spec* merge, int pdl, void* stream,
+                        int* status) {
+  return grouped_gemm_impl(groups, ngroups, w_rows, K, a_kplanes, epilogue, block_n, ksplit,
+                           split_stride, group_blocks, merge, stream, status, pdl);
+}
+}  // namespace fus
 
 extern "C" int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
                                 int a_kplanes, int epilogue, int block_n, int ksplit,
@@ -554,7 +599,7 @@ extern "C" int fus_grouped_gemm_merge(const fus_gemm_group* groups, int ngroups,
 static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
                              int a_kplanes, int epilogue, int block_n, int ksplit,
                              long split_stride, int group_blocks, const fus_merge_spec* merge,
-                             void* stream, int* status) {
+                             void* stream, int* status, int pdl) {
   if (!groups || ngroups < 1 || ngroups > 2)
     return set_error(FUS_E_INVALID, "ngroups must be 1 or 2");
   if (K <= 0 || K % kBK) return set_error(FUS_E_INVALID, "K=%d must be a positive multiple of 64", K);
@@ -580,6 +625,7 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
   a.m_tiles = w_rows / (128 * MTv);
   a.split_stride = split_stride;
   a.status = status;
+  a.pdl = pdl;
   if (merge) {
     a.mg.counters = merge->counters;
     a.mg.parts = merge->parts;

@@ -21,6 +21,15 @@ int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t
                       uint32_t box_inner, uint32_t box_rows);
 int num_sms();
 
+// Grouped GEMM entry used inside the library with programmatic dependent launch:
+// pdl = 0 plain launch; 1 launched early, every thread waits for the predecessor before
+// reading anything; 2 launched early, the dispatch layout is older than the predecessor
+// so weight tiles are prefetched before waiting (token rows are loaded after the wait).
+int grouped_gemm_launch(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
+                        int a_kplanes, int epilogue, int block_n, int ksplit, long split_stride,
+                        int group_blocks, const fus_merge_spec* merge, int pdl, void* stream,
+                        int* status);
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }

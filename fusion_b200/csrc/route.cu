@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   const int nv = H >> 3;
   const bool writer = blockIdx.x == 0;
   const int e0 = blockIdx.x * kRouteExperts;
+  pdl_allow_dependents();  // the w13 GEMM may become resident and set up meanwhile
   // this expert's weight planes for up to 4 chunks per thread are loaded up front (all
   // in flight at once) while the CTA normalises
   constexpr int kMaxChunks = 4;  // H <= 4 * 8 * 256 = 8192

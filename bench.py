@@ -196,6 +196,114 @@ class ClockSampler:
 # -------------------------------------------------------------------------------------
 # GPU arm
 # -------------------------------------------------------------------------------------
+def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks) -> None:
+    """N > 1: expert parallelism over NCCL (fusion_b200.ep). Rank g holds experts
+    [32g, 32g+32) at 8 GPUs; every rank routes its own T tokens (weak scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from fusion_b200 import ops, synth, traffic
+    from fusion_b200.ep import CudaEPBackend, ExpertParallelMoE, shard_weights
+
+    dims = synth.Dims()
+    w = shard_weights(SEED, rank, world, dims, "cuda")
+    be = CudaEPBackend(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"],
+                       w["w2s"], E=dims.E, rank=rank)
+    ep = ExpertParallelMoE(be)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    pk = traffic.peaks()
+
+    def measure(T: int, steps: int, warmup: int) -> dict:
+        h, r = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cuda")
+        for _ in range(warmup):
+            flush.zero_()
+            res = ep(h, r)
+        torch.cuda.synchronize()
+        ops.check_status()
+        barrier()
+        ms = []
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            res = ep(h, r)
+            b.record()
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+        barrier()
+        ms_step = max_over_ranks(statistics.fmean(ms))
+        # distinct experts over the whole job: union of every rank's routed ids
+        mask = torch.zeros(dims.E, dtype=torch.int32, device="cuda")
+        mask[res["topi"].reshape(-1).long()] = 1
+        dist.all_reduce(mask, op=dist.ReduceOp.MAX)
+        ne = int(mask.sum().item())
+        ks = traffic.block_kernels(world * T, ne, dims.H, dims.I, dims.E, dims.topk)
+        t_roof = traffic.chain_time_s(ks, pk) / world  # the job's work spread over W GPUs
+        f, byts = traffic.totals(ks)
+        return {"T_per_rank": T, "ms_per_step": ms_step, "us_per_block": ms_step * 1e3,
+                "tokens_per_s": world * T / (ms_step / 1e3), "distinct_experts": ne,
+                "roofline_us": t_roof * 1e6, "roofline_frac": t_roof / (ms_step / 1e3),
+                "algorithmic_GB_per_gpu": byts / world / 1e9}
+
+    with ClockSampler(local) as clk:
+        head = measure(HEADLINE_T, args.steps, max(args.warmup, 3))
+        regimes = {}
+        for T in [int(x) for x in args.regimes.split(",") if x.strip()]:
+            regimes[f"T{T}_per_rank"] = measure(T, max(5, min(args.steps, 20)), 3)
+
+    # e2e: pinned host inputs in, output out, every step
+    T = HEADLINE_T
+    hh, rh = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cpu")
+    hh, rh = hh.pin_memory(), rh.pin_memory()
+    out_h = torch.empty(T, dims.H, dtype=torch.bfloat16).pin_memory()
+    hd = torch.empty(T, dims.H, dtype=torch.bfloat16, device="cuda")
+    rd = torch.empty_like(hd)
+    evs = []
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        hd.copy_(hh, non_blocking=True)
+        rd.copy_(rh, non_blocking=True)
+        out_h.copy_(ep(hd, rd)["out"], non_blocking=True)
+        b.record()
+        b.synchronize()
+        evs.append(a.elapsed_time(b))
+    barrier()
+    e2e_ms = max_over_ranks(statistics.fmean(evs))
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": head["tokens_per_s"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded Irwin-Hall normals, GLM-5.2 shapes, random-init weights)",
+            "config": {"workload": f"decode_T{HEADLINE_T} per rank (BASELINE config 1), "
+                                   f"expert parallel over {world} GPUs",
+                       "T_per_rank": HEADLINE_T, "H": dims.H, "I": dims.I, "E": dims.E,
+                       "topk": dims.topk, "experts_per_gpu": dims.E // world,
+                       "l2": "flushed by a 512 MB write before every timed step",
+                       "parallelism": f"ep{world}",
+                       "timing": "eager EP step (NCCL all_to_all dispatch/combine), CUDA events"},
+            "us_per_block": head["us_per_block"],
+            "roofline": {"kernel": "whole EP block step (per GPU)", "bound": "hbm",
+                         "achieved": head["algorithmic_GB_per_gpu"] / (head["ms_per_step"] / 1e3),
+                         "peak": pk.hbm_gbs, "unit": "GB/s",
+                         "frac": head["roofline_frac"], "peak_source": pk.source,
+                         "traffic": None},
+            "block_roofline": {"roofline_us": head["roofline_us"], "frac": head["roofline_frac"]},
+            "cpu_baseline": None,
+            "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": hh.numel() * 4, "d2h_bytes_per_step": out_h.numel() * 2,
+                    "api": "fusion_b200.ep.ExpertParallelMoE.forward"},
+            "gpu_launches": 14 * args.steps,
+            "clocks": clk.summary(),
+            "regimes": regimes,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -226,6 +334,11 @@ def main() -> None:
         t = torch.tensor([v], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if world > 1:
+        run_ep(args, world, rank, local, barrier, max_over_ranks)
+        dist.destroy_process_group()
+        return
 
     dims = synth.Dims()
     w = synth.make_block_weights(SEED, dims, "cuda")
@@ -393,7 +506,7 @@ def main() -> None:
                        "T": HEADLINE_T, "H": dims.H, "I": dims.I, "E": dims.E,
                        "topk": dims.topk, "block_n": head["block_n"],
                        "l2": "flushed by a 512 MB write before every timed step",
-                       "parallelism": "single" if world == 1 else f"replica{world}",
+                       "parallelism": "single",
                        "timing": "CUDA-graph replay of the 8-launch block, CUDA events"},
             "us_per_block": head["us_per_block"],
             "block_roofline": {"roofline_us": head["roofline_us"],
@@ -409,8 +522,6 @@ def main() -> None:
             "regimes": regimes,
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

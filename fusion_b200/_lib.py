@@ -118,6 +118,9 @@ SIGNATURES: dict[str, tuple] = {
         i32,
         [C.POINTER(BlockDesc), vp, vp, i32, i32, vp, vp, vp, vp, vp, sz, vp, vp],
     ),
+    "fus_ep_plan": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp]),
+    "fus_ep_pack": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, i64, vp, vp, vp]),
+    "fus_ep_unpack": (i32, [vp, i64, i32, vp, i32, vp, i64, vp, vp]),
     "fus_synth_fill": (i32, [vp, i32, i64, i64, u64, f32, f32, vp]),
     "fus_synth_fill_host": (None, [vp, i32, i64, i64, u64, f32, f32]),
 }

@@ -237,6 +237,23 @@ def seed(o, src=None):
 
 
 # -------------------------------------------------------------------------------------
+def ep_plan(topi, E_loc: int, W: int, dest, leid, counts):
+    flat = topi.reshape(-1)
+    L.call("fus_ep_plan", _p(flat), flat.numel(), E_loc, W, _p(dest), _p(leid), _p(counts),
+           _stream(), _sp())
+
+
+def ep_pack(x, send_ids, n: int, div: int, leid, rows, leid_out):
+    L.call("fus_ep_pack", _p(x), _ld(x), x.shape[1], _p(send_ids), n, div, _p(leid), _p(rows),
+           _ld(rows), _p(leid_out), _stream(), _sp())
+
+
+def ep_unpack(rows, send_ids, n: int, y):
+    L.call("fus_ep_unpack", _p(rows), _ld(rows), rows.shape[1], _p(send_ids), n, _p(y), _ld(y),
+           _stream(), _sp())
+
+
+# -------------------------------------------------------------------------------------
 def synth_fill(t: torch.Tensor, seed: int, mean: float = 0.0, std: float = 1.0, offset: int = 0):
     """Fill ``t`` (bf16 or fp32, contiguous) with the seeded synthetic stream."""
     assert t.is_contiguous()

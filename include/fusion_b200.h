@@ -303,6 +303,24 @@ int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h, const void
                           void* workspace, size_t ws_bytes, void* stream, int* status);
 
 /* ---------------------------------------------------------------------------------
+ * Expert parallelism (no reference counterpart: the reference is single-GPU,
+ * log/LOG-00-plan-and-filter.md:41). Rank g owns experts [g*E_loc, (g+1)*E_loc); the
+ * row exchange is NCCL all_to_all (torch.distributed) between these steps.
+ * fus_ep_plan  : for each of the R (token, slot) pairs: dest rank = topi / E_loc,
+ *                leid = topi % E_loc, counts[W] = pairs per destination. W <= 64.
+ * fus_ep_pack  : rows[p] = x[send_ids[p] / div]; leid_out[p] = leid[send_ids[p]]
+ *                (leid may be NULL). send_ids = pairs stably sorted by dest, e.g.
+ *                fus_moe_align(dest, R, W, 1, ...).
+ * fus_ep_unpack: y[send_ids[p]] = rows[p]  (returned expert rows back to slot order)
+ * ------------------------------------------------------------------------------- */
+int fus_ep_plan(const int* topi, int R, int E_loc, int W, int* dest, int* leid, int* counts,
+                void* stream, int* status);
+int fus_ep_pack(const void* x, long ldx, int H, const int* send_ids, int n, int div,
+                const int* leid, void* rows, long ldr, int* leid_out, void* stream, int* status);
+int fus_ep_unpack(const void* rows, long ldr, int H, const int* send_ids, int n, void* y, long ldy,
+                  void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
  * Seeded synthetic inputs, bit-identical on the GPU and the host (no reference
  * counterpart: the reference draws torch.randn on the device, which a CPU oracle
  * cannot reproduce). Element i of a stream is

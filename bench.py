@@ -196,7 +196,8 @@ class ClockSampler:
 # -------------------------------------------------------------------------------------
 # GPU arm
 # -------------------------------------------------------------------------------------
-def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks) -> None:
+def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
+           stdout_fd: int) -> None:
     """N > 1: expert parallelism over NCCL (fusion_b200.ep). Rank g holds experts
     [32g, 32g+32) at 8 GPUs; every rank routes its own T tokens (weak scaling)."""
     import torch
@@ -214,6 +215,8 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks) -> 
     pk = traffic.peaks()
 
     def measure(T: int, steps: int, warmup: int) -> dict:
+        if rank == 0:
+            print(f"[bench ep{world}] T={T}/rank", file=sys.stderr, flush=True)
         h, r = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cuda")
         for _ in range(warmup):
             flush.zero_()
@@ -301,6 +304,8 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks) -> 
             "clocks": clk.summary(),
             "regimes": regimes,
         }
+        sys.stdout.flush()
+        os.dup2(stdout_fd, 1)
         print(json.dumps(line), flush=True)
 
 
@@ -322,6 +327,10 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
+        # NCCL may print to stdout; keep stdout for the one JSON line (restored below)
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
 
     def barrier():
@@ -336,7 +345,7 @@ def main() -> None:
         return float(t.item())
 
     if world > 1:
-        run_ep(args, world, rank, local, barrier, max_over_ranks)
+        run_ep(args, world, rank, local, barrier, max_over_ranks, saved_stdout)
         dist.destroy_process_group()
         return
 

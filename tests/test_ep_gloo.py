@@ -76,10 +76,11 @@ def test_ep_two_gloo_ranks_match_oracle(T_by_rank):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, T_by_rank, q)) for r in range(2)]
     for p in procs:
         p.start()
+    res = sorted(q.get(timeout=120) for _ in range(2))  # drain before joining
     for p in procs:
-        p.join(timeout=120)
+        p.join(timeout=60)
         assert p.exitcode == 0, f"rank exited with {p.exitcode}"
-    res = sorted(q.get(timeout=5) for _ in range(2))
+
     total_pairs = sum(T_by_rank) * D["topk"]
     assert sum(r[3] for r in res) == total_pairs  # every pair processed exactly once
     for rank, err, ids_ok, _ in res:

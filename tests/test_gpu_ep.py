@@ -108,10 +108,11 @@ def test_ep_two_nccl_ranks_match_block():
     ps = [ctx.Process(target=_two_rank_worker, args=(r, port, q)) for r in range(2)]
     for p in ps:
         p.start()
+    # drain before joining: a child cannot exit while its result is still in the pipe
+    outs = dict(q.get(timeout=240) for _ in range(2))
     for p in ps:
-        p.join(timeout=300)
+        p.join(timeout=60)
         assert p.exitcode == 0
-    outs = dict(q.get(timeout=5) for _ in range(2))
     w = synth.make_block_weights(404, D, DEV)
     blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"])
     for rank in range(2):

@@ -38,7 +38,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-block tokens/s & us at T=1/32/256/2048/8192, 1-8 B200, % of roofline"
 UNIT = "tokens/s"
 HEADLINE_T = 1
-REGIMES = [32, 256, 2048, 8192]
+REGIMES = ["32", "256", "2048", "8192", "8192z"]  # "z": Zipf(1.1) routing (config 4)
 SEED = 1
 FLUSH_BYTES = 512 * 2**20  # > 4x the 126 MB L2
 
@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["fusion", "reference"], default="fusion")
-    ap.add_argument("--regimes", default=",".join(map(str, REGIMES)),
+    ap.add_argument("--regimes", default=",".join(REGIMES),
                     help="extra T values measured besides the headline ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -251,7 +251,10 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
     with ClockSampler(local) as clk:
         head = measure(HEADLINE_T, args.steps, max(args.warmup, 3))
         regimes = {}
-        for T in [int(x) for x in args.regimes.split(",") if x.strip()]:
+        for x in [x.strip() for x in args.regimes.split(",") if x.strip()]:
+            if x.endswith("z"):
+                continue  # the skewed-routing regime is measured on one GPU
+            T = int(x)
             regimes[f"T{T}_per_rank"] = measure(T, max(5, min(args.steps, 20)), 3)
 
     # e2e: pinned host inputs in, output out, every step
@@ -358,8 +361,17 @@ def main() -> None:
     def launches_per_step(T: int) -> int:
         return 3 if T <= 16 else 8 + (2 if T * dims.topk > 8192 else 0)
 
-    def measure(T: int, steps: int, warmup: int) -> dict:
-        g, hin, rin, outs, _ = blk.capture(T)
+    blk_zipf = None
+
+    def measure(T: int, steps: int, warmup: int, zipf: bool = False) -> dict:
+        nonlocal blk_zipf
+        b = blk
+        if zipf:
+            if blk_zipf is None:
+                blk_zipf = MoEBlock(w["gamma"], w["gate_w"], synth.zipf_bias("cuda"), w["w13"],
+                                    w["w2"], w["w13s"], w["w2s"])
+            b = blk_zipf
+        g, hin, rin, outs, _ = b.capture(T)
         h, r = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cuda")
         hin.copy_(h)
         rin.copy_(r)
@@ -431,8 +443,11 @@ def main() -> None:
     with ClockSampler(local) as clk:
         head = measure(HEADLINE_T, args.steps, max(args.warmup, 3))
         regimes = {}
-        for T in [int(x) for x in args.regimes.split(",") if x.strip()]:
-            regimes[f"T{T}"] = measure(T, max(5, min(args.steps, 20)), 3)
+        for x in [x.strip() for x in args.regimes.split(",") if x.strip()]:
+            zipf = x.endswith("z")
+            T = int(x.rstrip("z"))
+            key = f"T{T}_zipf1.1" if zipf else f"T{T}"
+            regimes[key] = measure(T, max(5, min(args.steps, 20)), 3, zipf)
 
     # ---- dominant kernel roofline (w13 + SwiGLU grouped GEMM) ----
     kt, ch = kernel_times(HEADLINE_T)

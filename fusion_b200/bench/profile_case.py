@@ -1,0 +1,84 @@
+"""Small, self-contained grouped-GEMM launches for ncu captures.
+
+    python -m fusion_b200.bench.profile_case decode  [reps]
+    python -m fusion_b200.bench.profile_case prefill [reps]
+
+decode : the w13+SwiGLU and w2 launches of the decode block at T=1 — 8 routed experts
+         with one token each plus the shared expert (the same tile shapes, flags and
+         bytes per launch as the block), on a 16-expert weight stack (1.2 GB allocated).
+prefill: 16 experts x 256 tokens each (the per-expert load of T=8192 over 256 experts),
+         256-token tiles with two weight tiles per CTA.
+Each launch is timed with CUDA events; the line printed gives us and TB/s or TF/s.
+"""
+
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from .. import ops, synth
+
+
+def main(case: str, reps: int = 3) -> None:
+    H, I, E, K = 6144, 2048, 16, 8
+    w13 = synth.make("w13", (E, 2 * I, H), 1, "cuda")
+    w2 = synth.make("w2", (E, H, I), 1, "cuda")
+    w13s = synth.make("w13s", (2 * I, H), 1, "cuda")
+    w2s = synth.make("w2s", (H, I), 1, "cuda")
+    if case == "prefill":
+        T, bn = 512, 256
+        ids = (torch.arange(T * K, device="cuda") % E).view(T, K).to(torch.int32)
+    else:
+        T, bn = 1, 16
+        ids = torch.arange(K, device="cuda", dtype=torch.int32).view(1, K)
+    R = T * K
+    cap = (R + E * (bn - 1) + bn - 1) // bn * bn
+    s = torch.empty(cap, dtype=torch.int32, device="cuda")
+    e = torch.empty(cap // bn, dtype=torch.int32, device="cuda")
+    n = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.moe_align(ids, E, bn, s, e, n)
+    x = synth.make("h", (T, H), 1, "cuda")
+    act = torch.empty(cap, I, dtype=torch.bfloat16, device="cuda")
+    act_s = torch.empty(T, I, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
+    ys = torch.empty(T, H, dtype=torch.float32, device="cuda")
+    maxb = min(R, E) + R // bn
+    decode = case != "prefill"
+    ws = ops.GEMM_W_STREAM if decode else 0
+    if decode:  # rows gathered inside the GEMM, as the decode block does
+        g13 = [ops.gemm_group(w13, x, act, expert_ids=e, ntp=n, max_blocks=maxb, row_limit=cap,
+                              flags=ops.GEMM_SWIGLU_EXACT | ws, live_ids=s, live_limit=R,
+                              gather_ids=s, gather_div=K),
+               ops.gemm_group(w13s, x, act_s, max_blocks=1, row_limit=T,
+                              flags=ops.GEMM_SWIGLU_EXACT | ws)]
+    else:
+        xs = torch.empty(cap, H, dtype=torch.bfloat16, device="cuda")
+        ops.permute_rows(x, s, n, K, R, xs, cap)
+        g13 = [ops.gemm_group(w13, xs, act, expert_ids=e, ntp=n, max_blocks=maxb, row_limit=cap,
+                              flags=ops.GEMM_SWIGLU_EXACT, live_ids=s, live_limit=R)]
+    g2 = [ops.gemm_group(w2, act, y, expert_ids=e, ntp=n, max_blocks=maxb, row_map=s,
+                         row_limit=R, live_ids=s, live_limit=R, flags=ws)]
+    if decode:
+        g2.append(ops.gemm_group(w2s, act_s, ys, max_blocks=1, row_limit=T,
+                                 flags=ops.GEMM_OUT_F32 | ws))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(reps):
+        ev[0].record()
+        ops.grouped_gemm(g13, 2 * I, H, ops.FUS_EPI_SWIGLU, bn)
+        ev[1].record()
+        ops.grouped_gemm(g2, H, I, ops.FUS_EPI_BF16, bn)
+        ev[2].record()
+    torch.cuda.synchronize()
+    ops.check_status()
+    t13, t2 = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    ne = (K + 1) if decode else E
+    b13, b2 = ne * 2 * I * H * 2, ne * H * I * 2
+    f13, f2 = 2 * (R + (T if decode else 0)) * H * 2 * I, 2 * (R + (T if decode else 0)) * I * H
+    print(f"{case}: w13 {t13 * 1e3:.1f} us ({b13 / t13 / 1e9:.2f} TB/s weights, "
+          f"{f13 / t13 / 1e9:.1f} TF/s); w2 {t2 * 1e3:.1f} us ({b2 / t2 / 1e9:.2f} TB/s, "
+          f"{f2 / t2 / 1e9:.1f} TF/s)")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "decode", int(sys.argv[2]) if len(sys.argv) > 2 else 3)

@@ -83,3 +83,26 @@ def make_block_weights(base_seed: int, dims: Dims = Dims(), device="cuda",
 
 def make_inputs(base_seed: int, T: int, dims: Dims = Dims(), device="cuda"):
     return make("h", (T, dims.H), base_seed, device), make("r", (T, dims.H), base_seed, device)
+
+
+def zipf_bias_np(E: int, s: float, c: float, perm_seed: int):
+    """e_score_correction_bias giving Zipf(s) expert popularity:
+    b[pi(i)] = c * log(p_i), p_i = i^-s / sum, pi a seeded permutation (numpy, fp32)."""
+    import numpy as np
+
+    p = 1.0 / np.arange(1, E + 1, dtype=np.float64) ** s
+    p /= p.sum()
+    perm = np.random.default_rng(perm_seed).permutation(E)
+    b = np.empty(E, dtype=np.float64)
+    b[perm] = c * np.log(p)
+    return b.astype(np.float32)
+
+
+def zipf_bias(device="cpu") -> torch.Tensor:
+    """The calibrated config-4 bias (scale c fitted by tests/golden/calibrate_zipf.py)."""
+    import json
+    from pathlib import Path
+
+    cfg = json.loads((Path(__file__).resolve().parent / "zipf_bias.json").read_text())
+    b = zipf_bias_np(256, cfg["s"], cfg["c"], cfg["perm_seed"])
+    return torch.from_numpy(b).to(device)

@@ -38,7 +38,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "MoE-block tokens/s & us at T=1/32/256/2048/8192, 1-8 B200, % of roofline"
 UNIT = "tokens/s"
 HEADLINE_T = 1
-REGIMES = ["32", "256", "2048", "8192", "8192z"]  # "z": Zipf(1.1) routing (config 4)
+REGIMES = ["32", "256", "2048", "4096", "8192", "8192z"]  # "z": Zipf(1.1) routing (config 4)
 SEED = 1
 FLUSH_BYTES = 512 * 2**20  # > 4x the 126 MB L2
 

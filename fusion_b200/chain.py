@@ -18,7 +18,7 @@ from .block import BlockOutputs, MoEBlock
 
 
 class BlockChain:
-    def __init__(self, blk: MoEBlock, T: int, block_n: int = 0):
+    def __init__(self, blk: MoEBlock, T: int, block_n: int = 0, persist: bool = True):
         self.blk, self.T = blk, T
         H, I, E, K = blk.H, blk.I, blk.E, blk.topk
         self.bn = block_n or blk.block_n(T)
@@ -49,6 +49,7 @@ class BlockChain:
         self.logits = torch.empty(T, E, dtype=torch.float32, device=dev)
         self.outs: BlockOutputs = blk.alloc_outputs(T)
         self.shared = blk.desc.w13s is not None
+        self.np_flag = 0 if persist else ops.GEMM_NO_PERSIST
 
     def steps(self, h: torch.Tensor, r: torch.Tensor) -> list[tuple[str, Callable[[], None]]]:
         b, o = self.blk, self.outs
@@ -56,7 +57,7 @@ class BlockChain:
         keep = b._keep
         gamma, bias, w13, w2, w13s, w2s = keep[0], keep[1], keep[2], keep[3], keep[4], keep[5]
 
-        ws = ops.GEMM_W_STREAM if self.R / E <= bn else 0
+        ws = (ops.GEMM_W_STREAM if self.R / E <= bn else 0) | self.np_flag
         wss = ops.GEMM_W_STREAM if T <= bn else 0
 
         def w13_step():

@@ -85,7 +85,7 @@ extern "C" int fus_moe_block_pick_block_n(int T, int E, int topk) {
   if (per_expert <= 12) return 16;
   if (per_expert <= 24) return 32;
   if (per_expert <= 48) return 64;
-  if (per_expert <= 128) return 128;
+  if (per_expert <= 96) return 128;
   return 256;
 }
 

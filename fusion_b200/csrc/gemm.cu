@@ -479,10 +479,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+#include "gemm_persist.cuh"
+
 // ======================================================================================
 // host side
 // ======================================================================================
 namespace {
+
+template <int BN, int EPI>
+int launch_p(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t st) {
+  using Cfg = PersistCfg<BN>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(grouped_gemm_persistent<BN, EPI>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
+                                                cudaGetErrorString(attr_err));
+  grouped_gemm_persistent<BN, EPI><<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(maps[0], maps[1],
+                                                                          maps[2], maps[3], a);
+  return check_launch("grouped_gemm_persistent");
+}
+
+template <int EPI>
+int launch_persist(int bn, const CUtensorMap* maps, const GemmArgs& a, int grid,
+                   cudaStream_t st) {
+  switch (bn) {
+    case 64: return launch_p<64, EPI>(maps, a, grid, st);
+    case 128: return launch_p<128, EPI>(maps, a, grid, st);
+    case 256: return launch_p<256, EPI>(maps, a, grid, st);
+  }
+  return set_error(FUS_E_UNSUPPORTED, "persistent GEMM: block_n %d", bn);
+}
 
 template <int BN, int EPI, int MT>
 int launch_t(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t st) {
@@ -705,6 +734,19 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
   if (total > 0x7fffffffL) return set_error(FUS_E_UNSUPPORTED, "grid too large");
   a.units0 = (int)units[0];
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // prefill with many tiles: one persistent CTA per SM (each tile's loads overlap the
+  // previous epilogue); FUS_GEMM_NO_PERSIST in the first group's flags opts out. Beyond
+  // ~400 token blocks the statically strided CTAs drift apart over their many tiles and
+  // lose the L2 sharing that in-order CTA dispatch keeps (measured slower at T=8192).
+  const int sms = num_sms();
+  if (mt2 && epilogue != FUS_EPI_F32 && !merge && pdl == 0 && a.ksplit == 1 &&
+      total > 2L * sms && groups[0].max_blocks <= 400 &&
+      !(groups[0].flags & FUS_GEMM_NO_PERSIST) && !groups[0].gather_ids &&
+      (ngroups < 2 || !groups[1].gather_ids)) {
+    const int grid = (int)(total < sms ? total : sms);
+    return epilogue == FUS_EPI_SWIGLU ? launch_persist<FUS_EPI_SWIGLU>(block_n, maps, a, grid, st)
+                                      : launch_persist<FUS_EPI_BF16>(block_n, maps, a, grid, st);
+  }
   switch (epilogue) {
     case FUS_EPI_BF16: return launch_bn<FUS_EPI_BF16>(block_n, mt2, maps, a, (int)total, st);
     case FUS_EPI_SWIGLU: return launch_bn<FUS_EPI_SWIGLU>(block_n, mt2, maps, a, (int)total, st);

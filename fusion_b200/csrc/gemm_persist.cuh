@@ -1,0 +1,297 @@
+// Persistent variant of the grouped GEMM for prefill (two 128-row weight tiles per CTA,
+// FUS_EPI_BF16 / FUS_EPI_SWIGLU, no split-K, no fused merge). Included by gemm.cu.
+//
+// One CTA per SM walks the same unit list as the one-tile-per-CTA kernel (stride
+// gridDim.x). The producer's ring runs continuously across units, so the next unit's
+// weight and token tiles stream in while the epilogue drains the current accumulators;
+// the MMA of the next unit starts as soon as the epilogue has read TMEM. The epilogue
+// goes TMEM -> registers -> a 16 KB staging buffer (the ring stays busy) -> 16-byte
+// stores, 64 tokens (32 for fp32 output) at a time.
+#pragma once
+
+template <int BN>
+struct PersistCfg {
+  static constexpr int A_BYTES = 2 * kATileBytes;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGING_BYTES = 16 * 1024;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int TMEM_COLS = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);
+  static constexpr int SMEM_BYTES = RING_BYTES + STAGING_BYTES + 256 + 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+  static_assert(STAGES >= 2, "pipeline too shallow");
+};
+
+struct Unit {
+  int gi, mt, blk, expert;
+};
+
+// Decodes unit u (same order as the one-tile-per-CTA kernel); false when the unit has
+// no live rows.
+__device__ __forceinline__ bool decode_unit(const GemmArgs& a, int u, int BN, Unit& out,
+                                            bool report) {
+  int gi = 0;
+  if (u >= a.units0) {
+    gi = 1;
+    u -= a.units0;
+  }
+  const GroupDev& G = a.g[gi];
+  const int gsz_full = a.group_blocks * a.m_tiles;
+  const int grp = u / gsz_full;
+  const int rem = u - grp * gsz_full;
+  const int gsz = min(a.group_blocks, G.max_blocks - grp * a.group_blocks);
+  out.gi = gi;
+  out.mt = rem / gsz;
+  out.blk = grp * a.group_blocks + rem % gsz;
+  const int rows_used = G.ntp ? __ldg(G.ntp) : G.x_rows;
+  if (out.blk * BN >= rows_used) return false;
+  out.expert = G.expert_ids ? __ldg(G.expert_ids + out.blk) : 0;
+  if (out.expert < 0 || out.expert >= G.n_experts) {
+    if (report) raise_status(a.status, FUS_ERR_BAD_EXPERT);
+    return false;
+  }
+  return true;
+}
+
+// live token columns of a block (warp-wide; every lane gets the count)
+__device__ __forceinline__ int live_columns(const GroupDev& G, int pos0, int BN, int lane) {
+  int cnt = 0;
+  if (G.live_ids) {
+    for (int j = lane; j < BN; j += 32) cnt += __ldg(G.live_ids + pos0 + j) < G.live_limit;
+  } else if (lane == 0) {
+    cnt = min(BN, G.x_rows - pos0);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  return cnt;
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_persistent(const __grid_constant__ CUtensorMap ta0,
+                            const __grid_constant__ CUtensorMap ta1,
+                            const __grid_constant__ CUtensorMap tb0,
+                            const __grid_constant__ CUtensorMap tb1,
+                            const __grid_constant__ GemmArgs args) {
+  using Cfg = PersistCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sA = smem_u32(smem);
+  const uint32_t sB = sA + STAGES * Cfg::A_BYTES;
+  uint8_t* staging = smem + Cfg::RING_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_empty = smem_u32(bars + STAGES);
+  const uint32_t bar_acc_full = smem_u32(bars + 2 * STAGES);
+  const uint32_t bar_acc_empty = smem_u32(bars + 2 * STAGES + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long total = (long)args.units0 + (long)args.g[1].max_blocks * args.m_tiles;
+  const int nk = args.ksteps_total;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_acc_full, 1);
+    mbar_init(bar_acc_empty, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&ta0);
+    tma_prefetch_desc(&tb0);
+    tma_prefetch_desc(&ta1);
+    tma_prefetch_desc(&tb1);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: one continuous ring over all units ----------------
+      const uint64_t pol_x = policy_evict_last();
+      uint32_t c = 0;
+      bool stop = false;
+      for (long uu = blockIdx.x; uu < total && !stop; uu += gridDim.x) {
+        Unit un;
+        if (!decode_unit(args, (int)uu, BN, un, true)) continue;
+        const GroupDev& G = args.g[un.gi];
+        const CUtensorMap* tma_a = un.gi ? &ta1 : &ta0;
+        const CUtensorMap* tma_b = un.gi ? &tb1 : &tb0;
+        const uint64_t pol_w = (G.flags & FUS_GEMM_W_STREAM) ? policy_evict_first()
+                                                             : policy_evict_normal();
+        const int ebase = un.expert * args.w_rows;
+        int a_row0, a_row1;
+        if (EPI == FUS_EPI_SWIGLU) {
+          a_row0 = ebase + un.mt * 128;
+          a_row1 = ebase + (args.w_rows >> 1) + un.mt * 128;
+        } else {
+          a_row0 = ebase + un.mt * 256;
+          a_row1 = a_row0 + 128;
+        }
+        const int pos0 = un.blk * BN;
+        for (int i = 0; i < nk; ++i, ++c) {
+          const int s = c % STAGES;
+          const uint32_t r = c / STAGES;
+          if (!mbar_wait_bounded(bar_empty + 8 * s, (r & 1u) ^ 1u, abort_flag, args.status)) {
+            stop = true;
+            break;
+          }
+          const uint32_t full = bar_full + 8 * s;
+          const int kk = i * kBK;
+          mbar_arrive_expect_tx(full, Cfg::STAGE_BYTES);
+          const uint32_t a_dst = sA + s * Cfg::A_BYTES;
+          tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
+          tma_load_2d(a_dst + kATileBytes, tma_a, full, kk, a_row1, pol_w);
+          tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, pos0, pol_x);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    uint32_t c = 0, t = 0;
+    bool stop = false;
+    for (long uu = blockIdx.x; uu < total && !stop; uu += gridDim.x) {
+      Unit un;
+      if (!decode_unit(args, (int)uu, BN, un, false)) continue;
+      const int n_live = live_columns(args.g[un.gi], un.blk * BN, BN, lane);
+      const int n_mma = max(16, (n_live + 15) & ~15);
+      if (lane == 0) {
+        if (!mbar_wait_bounded(bar_acc_empty, (t & 1u) ^ 1u, abort_flag, args.status)) {
+          stop = true;
+        } else {
+          tc_fence_after();
+          const uint32_t idesc = idesc_bf16_f32(128, n_mma);
+          for (int i = 0; i < nk; ++i, ++c) {
+            const int s = c % STAGES;
+            const uint32_t r = c / STAGES;
+            if (!mbar_wait_bounded(bar_full + 8 * s, r & 1u, abort_flag, args.status)) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = sA + s * Cfg::A_BYTES;
+            const uint32_t b_base = sB + s * Cfg::B_BYTES;
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t bdesc = sw128_desc(b_base + 32 * k);
+              tc_mma_bf16(tmem, sw128_desc(a_base + 32 * k), bdesc, idesc, (i | k) != 0);
+              tc_mma_bf16(tmem + BN, sw128_desc(a_base + kATileBytes + 32 * k), bdesc, idesc,
+                          (i | k) != 0);
+            }
+            tc_commit(bar_empty + 8 * s);
+          }
+          tc_commit(bar_acc_full);
+        }
+      }
+      stop = __shfl_sync(0xffffffffu, (int)stop, 0);
+      ++t;
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q4 = warp & 3;
+    const int m = q4 * 32 + lane;
+    const int et = threadIdx.x - 64;
+    const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+    uint32_t t = 0;
+    for (long uu = blockIdx.x; uu < total; uu += gridDim.x) {
+      Unit un;
+      if (!decode_unit(args, (int)uu, BN, un, false)) continue;
+      const GroupDev& G = args.g[un.gi];
+      const int pos0 = un.blk * BN;
+      const int n_live = live_columns(G, pos0, BN, lane);
+      const int n_mma = max(16, (n_live + 15) & ~15);
+      if (et == 0) *ep_ok = mbar_wait_bounded(bar_acc_full, t & 1u, abort_flag, args.status);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!*ep_ok) break;
+      tc_fence_after();
+      const bool exact = G.flags & FUS_GEMM_SWIGLU_EXACT;
+      const bool out32 = (EPI == FUS_EPI_BF16) && (G.flags & FUS_GEMM_OUT_F32);
+      const int CH = out32 ? 32 : 64;  // tokens per staging round (16 KB)
+      constexpr int PASSES = (EPI == FUS_EPI_SWIGLU) ? 1 : 2;
+      for (int pass = 0; pass < PASSES; ++pass) {
+        const int col0 = (EPI == FUS_EPI_SWIGLU) ? un.mt * 128 : (un.mt * 2 + pass) * 128;
+        for (int c0 = 0; c0 < n_mma; c0 += CH) {
+          const int cw = min(CH, n_mma - c0);
+          for (int c = 0; c < cw; c += 16) {
+            float v[16];
+            if (EPI == FUS_EPI_SWIGLU) {
+              float u[16];
+              tmem_ld16(lane_base + (uint32_t)(c0 + c), v);
+              tmem_ld16(lane_base + (uint32_t)(BN + c0 + c), u);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float g = exact ? v[j] : round_bf(v[j]);
+                const float up = exact ? u[j] : round_bf(u[j]);
+                v[j] = (g / (1.0f + expf(-g))) * up;
+              }
+            } else {
+              tmem_ld16(lane_base + (uint32_t)(pass * BN + c0 + c), v);
+              if (G.row_scale) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int pos = pos0 + c0 + c + j;
+                  const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
+                  v[j] *= row < G.row_limit ? __ldg(G.row_scale + row) : 0.f;
+                }
+              }
+            }
+            if (out32) {
+              float* st = reinterpret_cast<float*>(staging);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) st[(c + j) * 128 + m] = v[j];
+            } else {
+              __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) st[(c + j) * 128 + m] = __float2bfloat16_rn(v[j]);
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const int nrow = min(cw, n_live - c0);
+          const int vec_per_row = out32 ? 32 : 16;  // 16-byte vectors per 128 features
+          for (int it = et; it < nrow * vec_per_row; it += 128) {
+            const int j = it / vec_per_row, q = it % vec_per_row;
+            const int pos = pos0 + c0 + j;
+            const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
+            if (row >= G.row_limit) continue;
+            if (out32) {
+              const uint4 val = reinterpret_cast<const uint4*>(staging)[j * 32 + q];
+              *reinterpret_cast<uint4*>(reinterpret_cast<float*>(G.out) + (long)row * G.ldo +
+                                        col0 + q * 4) = val;
+            } else {
+              const uint4 val = reinterpret_cast<const uint4*>(staging)[j * 16 + q];
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(G.out) +
+                                        (long)row * G.ldo + col0 + q * 8) = val;
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+      }
+      // accumulators read: hand TMEM back to the MMA warp for the next unit
+      tc_fence_before();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (et == 0) mbar_arrive(bar_acc_empty);
+      ++t;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}

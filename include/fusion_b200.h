@@ -54,6 +54,9 @@ extern "C" {
                                   /* load it L2 evict-first (decode); default evict-normal */
 #define FUS_GEMM_MERGE 0x8        /* this group's rows take part in the fused merge of     */
                                   /* fus_grouped_gemm_merge (token = row / token_div)      */
+#define FUS_GEMM_NO_PERSIST 0x10  /* (first group) keep one tile per CTA; by default wide- */
+                                  /* tile launches with many tiles run one persistent CTA  */
+                                  /* per SM that overlaps each epilogue with the next loads */
 
 int fus_version(void);
 const char* fus_last_error(void);

@@ -119,6 +119,8 @@ SIGNATURES: dict[str, tuple] = {
         [C.POINTER(BlockDesc), vp, vp, i32, i32, vp, vp, vp, vp, vp, sz, vp, vp],
     ),
     "fus_ep_plan": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp]),
+    "fus_ep_dispatch_small": (i32, [vp, i64, i32, vp, i32, i32, i32, i32, i32, vp, i64, vp, vp, vp,
+                                    vp]),
     "fus_ep_pack": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, i64, vp, vp, vp]),
     "fus_ep_unpack": (i32, [vp, i64, i32, vp, i32, vp, i64, vp, vp]),
     "fus_synth_fill": (i32, [vp, i32, i64, i64, u64, f32, f32, vp]),

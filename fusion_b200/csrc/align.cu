@@ -31,7 +31,7 @@ constexpr int kAlignMaxE = 512;
 // Ranks the (up to 1024) elements [base, base+1024) of `ids` against each other and
 // against earlier chunks (`cursor[e]` = elements of expert e already ranked).
 // wcnt is [32][E] shared scratch. Returns (through rank_out) the stable rank, -1 for
-// elements that are out of range or carry an invalid expert.
+// elements that are out of range, holes (negative ids) or carry an invalid expert.
 __device__ void rank_chunk(const int* __restrict__ ids, int base, int numel, int E, int* wcnt,
                            int* cursor, int& my_e, int& my_rank, int* status) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -39,9 +39,11 @@ __device__ void rank_chunk(const int* __restrict__ ids, int base, int numel, int
   int e = -1;
   if (i < numel) {
     e = ids[i];
-    if (e < 0 || e >= E) {
+    if (e >= E) {
       raise_status(status, FUS_ERR_BAD_EXPERT);
       e = -1;
+    } else if (e < 0) {
+      e = -1;  // a hole: no pair at this flat index (expert-parallel slot buffers)
     }
   }
   for (int j = tid; j < kAlignWarps * E; j += kAlignThreads) wcnt[j] = 0;

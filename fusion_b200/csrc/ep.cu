@@ -68,6 +68,47 @@ __global__ void ep_unpack_kernel(const __nv_bfloat16* __restrict__ rows, long ld
   }
 }
 
+// one CTA: slots by a stable rank per destination, then one warp per used slot copies
+__global__ void __launch_bounds__(1024)
+    ep_dispatch_small_kernel(const __nv_bfloat16* __restrict__ x, long ldx, int H,
+                             const int* __restrict__ topi, int R, int topk, int E_loc, int W,
+                             int S, __nv_bfloat16* __restrict__ rows, long ldr,
+                             int* __restrict__ leid_out, int* __restrict__ slot_of_pair,
+                             int* status) {
+  __shared__ int dst_s[1024];
+  __shared__ int slot_s[1024];
+  for (int i = threadIdx.x; i < W * S; i += blockDim.x) leid_out[i] = -1;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) {
+    const int e = topi[i];
+    int d = e / E_loc;
+    if (e < 0 || d >= W) {
+      raise_status(status, FUS_ERR_BAD_EXPERT);
+      d = -1;
+    }
+    dst_s[i] = d;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < R; i += blockDim.x) {
+    const int d = dst_s[i];
+    int rank = 0;
+    for (int j = 0; j < i; ++j) rank += dst_s[j] == d;
+    const int slot = d < 0 || rank >= S ? -1 : d * S + rank;
+    if (d >= 0 && rank >= S) raise_status(status, FUS_ERR_CAPACITY);
+    slot_s[i] = slot;
+    slot_of_pair[i] = slot < 0 ? 0 : slot;
+    if (slot >= 0) leid_out[slot] = topi[i] - d * E_loc;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < R; i += blockDim.x >> 5) {
+    const int slot = slot_s[i];
+    if (slot < 0) continue;
+    const uint4* s = reinterpret_cast<const uint4*>(x + (long)(i / topk) * ldx);
+    uint4* d = reinterpret_cast<uint4*>(rows + (long)slot * ldr);
+    for (int v = lane; v < (H >> 3); v += 32) d[v] = __ldg(s + v);
+  }
+}
+
 static int row_grid(int n) {
   int g = ceil_div(n, 8);
   const int cap = num_sms() * 8;
@@ -109,4 +150,19 @@ extern "C" int fus_ep_unpack(const void* rows, long ldr, int H, const int* send_
   ep_unpack_kernel<<<row_grid(n), 256, 0, as_stream(stream)>>>(
       (const __nv_bfloat16*)rows, ldr, H, send_ids, n, (__nv_bfloat16*)y, ldy);
   return check_launch("ep_unpack");
+}
+
+extern "C" int fus_ep_dispatch_small(const void* x, long ldx, int H, const int* topi, int T,
+                                     int topk, int E_loc, int W, int S, void* rows, long ldr,
+                                     int* leid_out, int* slot_of_pair, void* stream, int* status) {
+  const int R = T * topk;
+  if (!x || !topi || !rows || !leid_out || !slot_of_pair || T < 0 || topk < 1 || E_loc < 1 ||
+      W < 1 || W > kEpMaxRanks || S < R || H <= 0 || H % 8 || ldx % 8 || ldr % 8 ||
+      !aligned16(x) || !aligned16(rows))
+    return set_error(FUS_E_INVALID, "ep_dispatch_small: bad args");
+  if (R > 1024) return set_error(FUS_E_UNSUPPORTED, "ep_dispatch_small: T*topk=%d > 1024", R);
+  ep_dispatch_small_kernel<<<1, 1024, 0, as_stream(stream)>>>(
+      (const __nv_bfloat16*)x, ldx, H, topi, R, topk, E_loc, W, S, (__nv_bfloat16*)rows, ldr,
+      leid_out, slot_of_pair, status);
+  return check_launch("ep_dispatch_small");
 }

@@ -67,7 +67,54 @@ class ExpertParallelMoE:
         out = be.merge(y_flat, topw, h1, ys)
         return {"out": out, "h1": h1, "topw": topw, "topi": topi, "rows_in": n_in}
 
+    def forward_fixed(self, h: torch.Tensor, r: torch.Tensor) -> dict:
+        """Small-batch step with fixed split sizes (no host synchronisation, capturable in
+        a CUDA graph): every rank sends every peer a block of S = T*topk slots, unused
+        slots carry local expert -1 (holes the owner skips)."""
+        be = self.be
+        h1, x2, topw, topi = be.route(h, r)
+        T, K = topi.shape
+        S = T * K
+        send_rows, send_leid, slots = be.dispatch_fixed(x2, topi, self.W, S)
+        recv_rows = torch.empty_like(send_rows)
+        recv_leid = torch.empty_like(send_leid)
+        eq = [S] * self.W
+        self._a2a(recv_rows, send_rows, eq, eq)
+        self._a2a(recv_leid, send_leid, eq, eq)
+        y_recv = be.local_experts_holes(recv_rows, recv_leid)
+        y_ret = torch.empty_like(y_recv)
+        self._a2a(y_ret, y_recv, eq, eq)
+        y_flat = be.gather_rows(y_ret, slots, T * K)
+        ys = be.shared(x2)
+        out = be.merge(y_flat, topw, h1, ys)
+        return {"out": out, "h1": h1, "topw": topw, "topi": topi}
+
     __call__ = forward
+
+
+class EPDecodeGraph:
+    """`forward_fixed` for a fixed T recorded in a CUDA graph (NCCL all_to_all included);
+    copy inputs into `h` / `r`, call `replay()`, read `out`."""
+
+    def __init__(self, ep: ExpertParallelMoE, T: int, H: int, device):
+        self.ep = ep
+        self.h = torch.zeros(T, H, dtype=torch.bfloat16, device=device)
+        self.r = torch.zeros_like(self.h)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                ep.forward_fixed(self.h, self.r)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.res = ep.forward_fixed(self.h, self.r)
+        self.out = self.res["out"]
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
 
 
 class CudaEPBackend:
@@ -145,6 +192,44 @@ class CudaEPBackend:
                             row_map=sorted_ids, row_limit=n, flags=ws, live_ids=sorted_ids,
                             live_limit=n)
         ops.grouped_gemm([g2], H, I, ops.FUS_EPI_BF16, bn)
+        return y
+
+    def dispatch_fixed(self, x2, topi, W: int, S: int):
+        rows = torch.empty(W * S, x2.shape[1], dtype=x2.dtype, device=self.dev)
+        leid = torch.empty(W * S, dtype=torch.int32, device=self.dev)
+        slots = torch.empty(topi.numel(), dtype=torch.int32, device=self.dev)
+        ops.ep_dispatch_small(x2, topi, self.E_loc, W, S, rows, leid, slots)
+        return rows, leid, slots
+
+    def local_experts_holes(self, rows, leid):
+        """Expert rows for a slot buffer with holes (local expert -1): the token rows are
+        gathered by dispatch position inside the w13 GEMM (no permutation pass)."""
+        n, H = rows.shape
+        I, E, bn = self.I, self.E_loc, 16
+        y = torch.empty(n, H, dtype=torch.bfloat16, device=self.dev)
+        cap = (n + E * (bn - 1) + bn - 1) // bn * bn
+        sorted_ids = torch.empty(cap, dtype=torch.int32, device=self.dev)
+        eids = torch.empty(cap // bn, dtype=torch.int32, device=self.dev)
+        ntp = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        ops.moe_align(leid.view(n, 1), E, bn, sorted_ids, eids, ntp)
+        act = torch.empty(cap, I, dtype=torch.bfloat16, device=self.dev)
+        maxb = min(min(n, E) + n // bn, cap // bn)
+        ws = ops.GEMM_W_STREAM
+        g = ops.gemm_group(self.w13, rows, act, expert_ids=eids, ntp=ntp, max_blocks=maxb,
+                           row_limit=cap, flags=ops.GEMM_SWIGLU_EXACT | ws,
+                           live_ids=sorted_ids, live_limit=n, gather_ids=sorted_ids,
+                           gather_div=1)
+        ops.grouped_gemm([g], 2 * I, H, ops.FUS_EPI_SWIGLU, bn)
+        g2 = ops.gemm_group(self.w2, act, y, expert_ids=eids, ntp=ntp, max_blocks=maxb,
+                            row_map=sorted_ids, row_limit=n, flags=ws, live_ids=sorted_ids,
+                            live_limit=n)
+        ops.grouped_gemm([g2], H, I, ops.FUS_EPI_BF16, bn)
+        return y
+
+    def gather_rows(self, y_ret, slots, R: int):
+        y = torch.empty(R, y_ret.shape[1], dtype=y_ret.dtype, device=self.dev)
+        n = torch.full((1,), R, dtype=torch.int32, device=self.dev)
+        ops.permute_rows(y_ret, slots, n, 1, y_ret.shape[0], y, R)
         return y
 
     def unpack(self, ret, send_ids, R: int):

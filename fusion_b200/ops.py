@@ -243,6 +243,12 @@ def ep_plan(topi, E_loc: int, W: int, dest, leid, counts):
            _stream(), _sp())
 
 
+def ep_dispatch_small(x, topi, E_loc: int, W: int, S: int, rows, leid_out, slot_of_pair):
+    T, K = topi.shape
+    L.call("fus_ep_dispatch_small", _p(x), _ld(x), x.shape[1], _p(topi), T, K, E_loc, W, S,
+           _p(rows), _ld(rows), _p(leid_out), _p(slot_of_pair), _stream(), _sp())
+
+
 def ep_pack(x, send_ids, n: int, div: int, leid, rows, leid_out):
     L.call("fus_ep_pack", _p(x), _ld(x), x.shape[1], _p(send_ids), n, div, _p(leid), _p(rows),
            _ld(rows), _p(leid_out), _stream(), _sp())

@@ -109,6 +109,8 @@ int fus_router_topk(const float* partial, int nsplit, const float* bias, float* 
  *   stable sort of the flat (token*topk+k) indices by expert, each expert's run
  *   padded to a multiple of block_m with the sentinel `numel`;
  *   expert_ids[b] = expert of block b; ntp[0] = padded total.
+ * Negative ids are holes: their flat index is simply not placed (no error); ids >= E
+ * raise FUS_ERR_BAD_EXPERT. The pad sentinel stays `numel`.
  * sorted_cap >= numel + E*(block_m-1) and blocks_cap >= sorted_cap/block_m are
  * always enough. Entries past ntp[0] are left untouched. `workspace` of
  * fus_moe_align_workspace(numel, E) bytes (may be 0 for small numel). E <= 512.
@@ -318,6 +320,13 @@ int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h, const void
  * ------------------------------------------------------------------------------- */
 int fus_ep_plan(const int* topi, int R, int E_loc, int W, int* dest, int* leid, int* counts,
                 void* stream, int* status);
+/* Fixed-slot dispatch for small batches (T*topk <= 1024), no host synchronisation: the
+ * send buffer has W blocks of S slots (S >= T*topk); pair i = (t, k) with destination d
+ * takes slot d*S + (its stable rank among the pairs to d). Writes rows[slot] =
+ * x[t], leid_out[slot] = local expert (-1 in unused slots), slot_of_pair[i]. */
+int fus_ep_dispatch_small(const void* x, long ldx, int H, const int* topi, int T, int topk,
+                          int E_loc, int W, int S, void* rows, long ldr, int* leid_out,
+                          int* slot_of_pair, void* stream, int* status);
 int fus_ep_pack(const void* x, long ldx, int H, const int* send_ids, int n, int div,
                 const int* leid, void* rows, long ldr, int* leid_out, void* stream, int* status);
 int fus_ep_unpack(const void* rows, long ldr, int H, const int* send_ids, int n, void* y, long ldy,

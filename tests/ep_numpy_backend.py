@@ -46,6 +46,32 @@ class NumpyEPBackend:
             y[i] = O.bf16(O.silu_and_mul(hh) @ w2.T)[0]
         return _bf(y)
 
+    def dispatch_fixed(self, x2, topi, W: int, S: int):
+        t = topi.reshape(-1).numpy()
+        K = topi.shape[1]
+        dest = t // self.E_loc
+        rows = torch.zeros(W * S, x2.shape[1], dtype=x2.dtype)
+        leid = torch.full((W * S,), -1, dtype=torch.int32)
+        slots = torch.zeros(t.size, dtype=torch.int32)
+        used = [0] * W
+        for i, d in enumerate(dest):
+            slot = d * S + used[d]
+            used[d] += 1
+            rows[slot] = x2[i // K]
+            leid[slot] = int(t[i] % self.E_loc)
+            slots[i] = slot
+        return rows, leid, slots
+
+    def local_experts_holes(self, rows, leid):
+        keep = torch.nonzero(leid >= 0).flatten()
+        y = torch.zeros(rows.shape[0], rows.shape[1], dtype=torch.bfloat16)
+        if keep.numel():
+            y[keep] = self.local_experts(rows[keep], leid[keep])
+        return y
+
+    def gather_rows(self, y_ret, slots, R: int):
+        return y_ret[slots.long()].contiguous()
+
     def unpack(self, ret, send_ids, R: int):
         y = torch.empty(R, ret.shape[1], dtype=ret.dtype)
         y[send_ids.long()] = ret

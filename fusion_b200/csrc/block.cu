@@ -48,7 +48,10 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   L.max_blocks = (L.R < E ? L.R : E) + L.R / bn;
   if (L.max_blocks > L.blocks_cap) L.max_blocks = L.blocks_cap;
   L.nsplit = fus_router_nsplit(T, H, E, d->nplanes);
-  size_t o = 0;
+  // the decode front end's ticket sits first, at the same offset for every T: no other
+  // buffer ever overlaps it, so it stays zero between calls of any size
+  size_t o = 256;
+  L.off_done = 0;
   auto take = [&](size_t bytes) {
     size_t at = o;
     o = align_up(o + bytes, 256);
@@ -67,7 +70,7 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   L.off_ys = take((size_t)T * H * 4);  // shared expert output, fp32
   L.tiles = fus_grouped_gemm_tiles(H, FUS_EPI_BF16, bn);
   L.off_cnt = take((size_t)T * L.tiles * 4);  // fused-merge arrival counters
-  L.off_done = take(16);                      // decode front end's ticket
+
   L.total = o + 256;  // base alignment slack
   return true;
 }

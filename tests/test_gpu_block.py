@@ -210,3 +210,15 @@ def test_route_small_equals_separate_kernels(weights_404, T):
     assert int(nb.item()) == n and torch.equal(sa[:n], sb[:n])
     assert torch.equal(ea[: n // bn], eb[: n // bn])
     assert int(done.sum().item()) == 0 and int(junk.abs().sum().item()) == 0
+
+
+def test_workspace_reused_across_sizes(weights_404):
+    """One workspace serves calls of different T (decode and prefill paths alternating)."""
+    blk = make_block(weights_404)
+    for seed, T in ((70, 24), (90, 2), (71, 300), (91, 2), (92, 1)):
+        h, r = synth.make_inputs(seed, T, D, DEV)
+        o = blk(h, r)
+        finish()
+        fresh = make_block(weights_404)(h, r)
+        finish()
+        assert torch.equal(o.out.view(torch.int16), fresh.out.view(torch.int16))

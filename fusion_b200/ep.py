@@ -75,6 +75,7 @@ class ExpertParallelMoE:
         h1, x2, topw, topi = be.route(h, r)
         T, K = topi.shape
         S = T * K
+        shared = be.shared_begin(x2) if hasattr(be, "shared_begin") else None
         send_rows, send_leid, slots = be.dispatch_fixed(x2, topi, self.W, S)
         recv_rows = torch.empty_like(send_rows)
         recv_leid = torch.empty_like(send_leid)
@@ -85,7 +86,7 @@ class ExpertParallelMoE:
         y_ret = torch.empty_like(y_recv)
         self._a2a(y_ret, y_recv, eq, eq)
         y_flat = be.gather_rows(y_ret, slots, T * K)
-        ys = be.shared(x2)
+        ys = be.shared_end(shared) if shared is not None else be.shared(x2)
         out = be.merge(y_flat, topw, h1, ys)
         return {"out": out, "h1": h1, "topw": topw, "topi": topi}
 
@@ -133,9 +134,44 @@ class CudaEPBackend:
             self.wa, self.nplanes = gate_w.contiguous(), 1
         self.dev = w13_local.device
 
+    def shared_begin(self, x2):
+        """Start the shared expert on a side stream (it overlaps the exchange and the
+        routed experts); `shared_end` joins it."""
+        side = torch.cuda.Stream(device=self.dev)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            ys = self.shared(x2)
+        return side, ys
+
+    def shared_end(self, handle):
+        side, ys = handle
+        torch.cuda.current_stream().wait_stream(side)
+        if ys is not None:
+            ys.record_stream(torch.cuda.current_stream())
+        return ys
+
     def route(self, h, r):
         T, H = h.shape
         bf = torch.bfloat16
+        if T <= 16 and self.E <= 256:
+            # decode: norm + router + top-k in one launch (its dispatch layout over all E
+            # experts is not needed here and goes to scratch)
+            h1 = torch.empty(T, H, dtype=bf, device=self.dev)
+            x2 = torch.empty(T, H, dtype=bf, device=self.dev)
+            logits = torch.empty(T, self.E, dtype=torch.float32, device=self.dev)
+            topw = torch.empty(T, self.topk, dtype=torch.float32, device=self.dev)
+            topi = torch.empty(T, self.topk, dtype=torch.int32, device=self.dev)
+            cap = T * self.topk + self.E * 15
+            cap = (cap + 15) // 16 * 16
+            if not hasattr(self, "_route_done"):
+                self._route_done = torch.zeros(4, dtype=torch.int32, device=self.dev)
+            sorted_ids = torch.empty(cap, dtype=torch.int32, device=self.dev)
+            eids = torch.empty(cap // 16, dtype=torch.int32, device=self.dev)
+            ntp = torch.empty(1, dtype=torch.int32, device=self.dev)
+            ops.route_small(h, r, self.gamma, self.wa, self.nplanes, self.bias, h1, x2, logits,
+                            topw, topi, 16, sorted_ids, eids, ntp, self._route_done,
+                            eps=self.eps, scale=self.scale)
+            return h1, x2, topw, topi
         h1, x2 = torch.empty(T, H, dtype=bf, device=self.dev), torch.empty(T, H, dtype=bf,
                                                                           device=self.dev)
         ops.add_rmsnorm(h, r, self.gamma, h1, x2, eps=self.eps)

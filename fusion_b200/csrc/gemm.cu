@@ -497,7 +497,7 @@ int launch_p(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t 
   });
   if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
                                                 cudaGetErrorString(attr_err));
-  grouped_gemm_persistent<BN, EPI><<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(maps[0], maps[1],
+  grouped_gemm_persistent<BN, EPI><<<grid, kPThreads, Cfg::SMEM_BYTES, st>>>(maps[0], maps[1],
                                                                           maps[2], maps[3], a);
   return check_launch("grouped_gemm_persistent");
 }
@@ -734,13 +734,12 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
   if (total > 0x7fffffffL) return set_error(FUS_E_UNSUPPORTED, "grid too large");
   a.units0 = (int)units[0];
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // prefill with many tiles: one persistent CTA per SM (each tile's loads overlap the
-  // previous epilogue); FUS_GEMM_NO_PERSIST in the first group's flags opts out. Beyond
-  // ~400 token blocks the statically strided CTAs drift apart over their many tiles and
-  // lose the L2 sharing that in-order CTA dispatch keeps (measured slower at T=8192).
+  // prefill with many tiles: one persistent CTA per SM (each tile's loads and MMAs
+  // overlap the previous tile's epilogue); FUS_GEMM_NO_PERSIST in the first group's
+  // flags opts out.
   const int sms = num_sms();
   if (mt2 && epilogue != FUS_EPI_F32 && !merge && pdl == 0 && a.ksplit == 1 &&
-      total > 2L * sms && groups[0].max_blocks <= 400 &&
+      total > 2L * sms &&
       !(groups[0].flags & FUS_GEMM_NO_PERSIST) && !groups[0].gather_ids &&
       (ngroups < 2 || !groups[1].gather_ids)) {
     const int grid = (int)(total < sms ? total : sms);

@@ -4,21 +4,30 @@
 // One CTA per SM walks the same unit list as the one-tile-per-CTA kernel (stride
 // gridDim.x). The producer's ring runs continuously across units, so the next unit's
 // weight and token tiles stream in while the epilogue drains the current accumulators;
-// the MMA of the next unit starts as soon as the epilogue has read TMEM. The epilogue
-// goes TMEM -> registers -> a 16 KB staging buffer (the ring stays busy) -> 16-byte
+// with block_n <= 128 the accumulators are double-buffered in TMEM, so the MMAs of the
+// next unit run while the epilogue drains the current one (with 256 the next unit's MMAs
+// wait for the drain). The epilogue
+// goes TMEM -> registers -> a 16 KB staging buffer per epilogue group -> 16-byte
 // stores, 64 tokens (32 for fp32 output) at a time.
 #pragma once
+
+// warp 0 TMA, warp 1 MMA, then two epilogue groups of four warps
+constexpr int kPEpiGroups = 2;
+constexpr int kPThreads = 64 + kPEpiGroups * 128;
 
 template <int BN>
 struct PersistCfg {
   static constexpr int A_BYTES = 2 * kATileBytes;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGING_BYTES = 16 * 1024;
+  static constexpr int STAGING_BYTES = 16 * 1024;  // per epilogue group
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int TMEM_COLS = pow2_at_least(2 * BN < 32 ? 32 : 2 * BN, 32);
-  static constexpr int SMEM_BYTES = RING_BYTES + STAGING_BYTES + 256 + 1024;
+  // two accumulator sets (double buffering) when they fit in the 512 TMEM columns
+  static constexpr int NBUF = 4 * BN <= 512 ? 2 : 1;
+  static constexpr int ACC_COLS = 2 * BN;
+  static constexpr int TMEM_COLS = pow2_at_least(NBUF * ACC_COLS < 32 ? 32 : NBUF * ACC_COLS, 32);
+  static constexpr int SMEM_BYTES = RING_BYTES + kPEpiGroups * STAGING_BYTES + 256 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static_assert(STAGES >= 2, "pipeline too shallow");
 };
@@ -68,7 +77,7 @@ __device__ __forceinline__ int live_columns(const GroupDev& G, int pos0, int BN,
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPThreads, 1)
     grouped_gemm_persistent(const __grid_constant__ CUtensorMap ta0,
                             const __grid_constant__ CUtensorMap ta1,
                             const __grid_constant__ CUtensorMap tb0,
@@ -81,15 +90,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   const uint32_t sA = smem_u32(smem);
   const uint32_t sB = sA + STAGES * Cfg::A_BYTES;
-  uint8_t* staging = smem + Cfg::RING_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + Cfg::STAGING_BYTES);
+  uint8_t* staging_all = smem + Cfg::RING_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging_all + kPEpiGroups * Cfg::STAGING_BYTES);
   const uint32_t bar_full = smem_u32(bars);
   const uint32_t bar_empty = smem_u32(bars + STAGES);
-  const uint32_t bar_acc_full = smem_u32(bars + 2 * STAGES);
-  const uint32_t bar_acc_empty = smem_u32(bars + 2 * STAGES + 1);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
+  const uint32_t bar_acc_full = smem_u32(bars + 2 * STAGES);       // [NBUF]
+  const uint32_t bar_acc_empty = smem_u32(bars + 2 * STAGES + 2);  // [NBUF]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [kPEpiGroups]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long total = (long)args.units0 + (long)args.g[1].max_blocks * args.m_tiles;
@@ -100,8 +109,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
-    mbar_init(bar_acc_full, 1);
-    mbar_init(bar_acc_empty, 1);
+    for (int b = 0; b < Cfg::NBUF; ++b) {
+      mbar_init(bar_acc_full + 8 * b, 1);
+      mbar_init(bar_acc_empty + 8 * b, kPEpiGroups);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&ta0);
@@ -168,8 +179,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!decode_unit(args, (int)uu, BN, un, false)) continue;
       const int n_live = live_columns(args.g[un.gi], un.blk * BN, BN, lane);
       const int n_mma = max(16, (n_live + 15) & ~15);
+      const uint32_t buf = t % Cfg::NBUF, use = t / Cfg::NBUF;  // accumulator set, its use
+      const uint32_t acc = tmem + buf * Cfg::ACC_COLS;
       if (lane == 0) {
-        if (!mbar_wait_bounded(bar_acc_empty, (t & 1u) ^ 1u, abort_flag, args.status)) {
+        if (!mbar_wait_bounded(bar_acc_empty + 8 * buf, (use & 1u) ^ 1u, abort_flag,
+                               args.status)) {
           stop = true;
         } else {
           tc_fence_after();
@@ -187,24 +201,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int k = 0; k < kBK / 16; ++k) {
               const uint64_t bdesc = sw128_desc(b_base + 32 * k);
-              tc_mma_bf16(tmem, sw128_desc(a_base + 32 * k), bdesc, idesc, (i | k) != 0);
-              tc_mma_bf16(tmem + BN, sw128_desc(a_base + kATileBytes + 32 * k), bdesc, idesc,
+              tc_mma_bf16(acc, sw128_desc(a_base + 32 * k), bdesc, idesc, (i | k) != 0);
+              tc_mma_bf16(acc + BN, sw128_desc(a_base + kATileBytes + 32 * k), bdesc, idesc,
                           (i | k) != 0);
             }
             tc_commit(bar_empty + 8 * s);
           }
-          tc_commit(bar_acc_full);
+          tc_commit(bar_acc_full + 8 * buf);
         }
       }
       stop = __shfl_sync(0xffffffffu, (int)stop, 0);
       ++t;
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..9: two groups of four) ----------------
+    // Each group of four warps covers the 128 TMEM lanes (warp % 4 = lane quadrant). With
+    // two passes (bf16/fp32 output) group g drains pass g; with SwiGLU the groups take
+    // alternate token chunks. Both arrive on acc_empty before the MMA warp reuses TMEM.
     const int q4 = warp & 3;
     const int m = q4 * 32 + lane;
-    const int et = threadIdx.x - 64;
-    const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+    const int eg = (threadIdx.x - 64) >> 7;
+    const int et = (threadIdx.x - 64) & 127;
+    const int bar_id = 1 + eg;
+    uint8_t* staging = staging_all + eg * Cfg::STAGING_BYTES;
+    volatile int* my_ok = ep_ok + eg;
     uint32_t t = 0;
     for (long uu = blockIdx.x; uu < total; uu += gridDim.x) {
       Unit un;
@@ -213,17 +233,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pos0 = un.blk * BN;
       const int n_live = live_columns(G, pos0, BN, lane);
       const int n_mma = max(16, (n_live + 15) & ~15);
-      if (et == 0) *ep_ok = mbar_wait_bounded(bar_acc_full, t & 1u, abort_flag, args.status);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (!*ep_ok) break;
+      const uint32_t buf = t % Cfg::NBUF, use = t / Cfg::NBUF;
+      const uint32_t lane_base =
+          tmem + buf * Cfg::ACC_COLS + ((uint32_t)(q4 * 32) << 16);
+      if (et == 0)
+        *my_ok = mbar_wait_bounded(bar_acc_full + 8 * buf, use & 1u, abort_flag, args.status);
+      named_bar_sync(bar_id, 128);
+      if (!*my_ok) break;
       tc_fence_after();
       const bool exact = G.flags & FUS_GEMM_SWIGLU_EXACT;
       const bool out32 = (EPI == FUS_EPI_BF16) && (G.flags & FUS_GEMM_OUT_F32);
       const int CH = out32 ? 32 : 64;  // tokens per staging round (16 KB)
       constexpr int PASSES = (EPI == FUS_EPI_SWIGLU) ? 1 : 2;
-      for (int pass = 0; pass < PASSES; ++pass) {
+      for (int pass = (PASSES == 2 ? eg : 0); pass < PASSES; pass += kPEpiGroups) {
         const int col0 = (EPI == FUS_EPI_SWIGLU) ? un.mt * 128 : (un.mt * 2 + pass) * 128;
-        for (int c0 = 0; c0 < n_mma; c0 += CH) {
+        const int c_first = PASSES == 2 ? 0 : eg * CH;
+        const int c_step = PASSES == 2 ? CH : kPEpiGroups * CH;
+        for (int c0 = c_first; c0 < n_mma; c0 += c_step) {
           const int cw = min(CH, n_mma - c0);
           for (int c = 0; c < cw; c += 16) {
             float v[16];
@@ -258,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 16; ++j) st[(c + j) * 128 + m] = __float2bfloat16_rn(v[j]);
             }
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+          named_bar_sync(bar_id, 128);
           const int nrow = min(cw, n_live - c0);
           const int vec_per_row = out32 ? 32 : 16;  // 16-byte vectors per 128 features
           for (int it = et; it < nrow * vec_per_row; it += 128) {
@@ -276,13 +302,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         (long)row * G.ldo + col0 + q * 8) = val;
             }
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+          named_bar_sync(bar_id, 128);
         }
       }
       // accumulators read: hand TMEM back to the MMA warp for the next unit
       tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) mbar_arrive(bar_acc_empty);
+      named_bar_sync(bar_id, 128);
+      if (et == 0) mbar_arrive(bar_acc_empty + 8 * buf);
       ++t;
     }
   }

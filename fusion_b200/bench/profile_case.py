@@ -2,12 +2,15 @@
 
     python -m fusion_b200.bench.profile_case decode  [reps]
     python -m fusion_b200.bench.profile_case prefill [reps]
+    python -m fusion_b200.bench.profile_case prefill32 [reps]
 
 decode : the w13+SwiGLU and w2 launches of the decode block at T=1 — 8 routed experts
          with one token each plus the shared expert (the same tile shapes, flags and
          bytes per launch as the block), on a 16-expert weight stack (1.2 GB allocated).
 prefill: 16 experts x 256 tokens each (the per-expert load of T=8192 over 256 experts),
          256-token tiles with two weight tiles per CTA.
+prefill32: the same on 32 experts (2.4 GB of weights; several tiles per SM, so the
+         persistent kernel's steady state dominates rather than its tail).
 Each launch is timed with CUDA events; the line printed gives us and TB/s or TF/s.
 """
 
@@ -21,13 +24,14 @@ from .. import ops, synth
 
 
 def main(case: str, reps: int = 3) -> None:
-    H, I, E, K = 6144, 2048, 16, 8
+    H, I, K = 6144, 2048, 8
+    E = 32 if case == "prefill32" else 16
     w13 = synth.make("w13", (E, 2 * I, H), 1, "cuda")
     w2 = synth.make("w2", (E, H, I), 1, "cuda")
     w13s = synth.make("w13s", (2 * I, H), 1, "cuda")
     w2s = synth.make("w2s", (H, I), 1, "cuda")
-    if case == "prefill":
-        T, bn = 512, 256
+    if case.startswith("prefill"):
+        T, bn = 32 * E, 256
         ids = (torch.arange(T * K, device="cuda") % E).view(T, K).to(torch.int32)
     else:
         T, bn = 1, 16
@@ -44,7 +48,7 @@ def main(case: str, reps: int = 3) -> None:
     y = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
     ys = torch.empty(T, H, dtype=torch.float32, device="cuda")
     maxb = min(R, E) + R // bn
-    decode = case != "prefill"
+    decode = not case.startswith("prefill")
     ws = ops.GEMM_W_STREAM if decode else 0
     if decode:  # rows gathered inside the GEMM, as the decode block does
         g13 = [ops.gemm_group(w13, x, act, expert_ids=e, ntp=n, max_blocks=maxb, row_limit=cap,
@@ -57,8 +61,13 @@ def main(case: str, reps: int = 3) -> None:
         ops.permute_rows(x, s, n, K, R, xs, cap)
         g13 = [ops.gemm_group(w13, xs, act, expert_ids=e, ntp=n, max_blocks=maxb, row_limit=cap,
                               flags=ops.GEMM_SWIGLU_EXACT, live_ids=s, live_limit=R)]
-    g2 = [ops.gemm_group(w2, act, y, expert_ids=e, ntp=n, max_blocks=maxb, row_map=s,
-                         row_limit=R, live_ids=s, live_limit=R, flags=ws)]
+    if decode:  # rows to pair order (the decode block merges from there)
+        g2 = [ops.gemm_group(w2, act, y, expert_ids=e, ntp=n, max_blocks=maxb, row_map=s,
+                             row_limit=R, live_ids=s, live_limit=R, flags=ws)]
+    else:  # rows stay in dispatch order (dense tile stores), as the prefill block does
+        y = torch.empty(cap, H, dtype=torch.bfloat16, device="cuda")
+        g2 = [ops.gemm_group(w2, act, y, expert_ids=e, ntp=n, max_blocks=maxb, row_limit=cap,
+                             live_ids=s, live_limit=R, flags=ws)]
     if decode:
         g2.append(ops.gemm_group(w2s, act_s, ys, max_blocks=1, row_limit=T,
                                  flags=ops.GEMM_OUT_F32 | ws))

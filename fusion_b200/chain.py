@@ -30,6 +30,7 @@ class BlockChain:
         self.max_blocks = min(min(R, E) + R // bn, cap // bn)
         self.nsplit = ops.router_nsplit(T, H, E, blk.nplanes)
         bf = torch.bfloat16
+        self.small = T <= 16 and E <= 256 and E % 2 == 0 and T * K <= 256 and blk.nplanes in (1, 3)
         self.x2 = torch.empty(T, H, dtype=bf, device=dev)
         self.partial = torch.empty(self.nsplit, T, E, dtype=torch.float32, device=dev)
         self.sorted = torch.empty(cap, dtype=torch.int32, device=dev)
@@ -37,15 +38,17 @@ class BlockChain:
         self.ntp = torch.zeros(1, dtype=torch.int32, device=dev)
         nws = ops.moe_align_workspace(R, E)
         self.align_ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
-        self.xs = None if T <= 16 else torch.empty(cap, H, dtype=bf, device=dev)
+        self.xs = None if self.small else torch.empty(cap, H, dtype=bf, device=dev)
         self.act = torch.empty(cap, I, dtype=bf, device=dev)
         self.act_s = torch.empty(T, I, dtype=bf, device=dev)
-        self.y = torch.empty(R, H, dtype=bf, device=dev)
+        # decode: y in pair order (fused merge); prefill: rows in dispatch order, stored
+        # over the permuted rows (dead after w13) and merged through pos_of
+        self.y = torch.empty(R, H, dtype=bf, device=dev) if self.small else None
+        self.pos_of = torch.empty(R, dtype=torch.int32, device=dev)
         self.ys = torch.empty(T, H, dtype=torch.float32, device=dev)
         self.tiles = ops.gemm_tiles(H, ops.FUS_EPI_BF16, bn)
         self.counters = torch.zeros(T * self.tiles, dtype=torch.int32, device=dev)
         self.done = torch.zeros(4, dtype=torch.int32, device=dev)
-        self.small = T <= 16 and E <= 256 and E % 2 == 0 and T * K <= 256
         self.logits = torch.empty(T, E, dtype=torch.float32, device=dev)
         self.outs: BlockOutputs = blk.alloc_outputs(T)
         self.shared = blk.desc.w13s is not None
@@ -78,10 +81,16 @@ class BlockChain:
 
         def w2_groups(merge: bool):
             mf = ops.GEMM_MERGE if merge else 0
-            gs = [ops.gemm_group(w2, self.act, self.y, expert_ids=self.eids, ntp=self.ntp,
-                                 max_blocks=self.max_blocks, row_map=self.sorted,
-                                 row_limit=self.R, flags=ws | mf, live_ids=self.sorted,
-                                 live_limit=self.R, token_div=K)]
+            if merge:
+                g0 = ops.gemm_group(w2, self.act, self.y, expert_ids=self.eids, ntp=self.ntp,
+                                    max_blocks=self.max_blocks, row_map=self.sorted,
+                                    row_limit=self.R, flags=ws | mf, live_ids=self.sorted,
+                                    live_limit=self.R, token_div=K)
+            else:
+                g0 = ops.gemm_group(w2, self.act, self.xs, expert_ids=self.eids, ntp=self.ntp,
+                                    max_blocks=self.max_blocks, row_limit=self.cap, flags=ws,
+                                    live_ids=self.sorted, live_limit=self.R)
+            gs = [g0]
             if self.shared:
                 gs.append(ops.gemm_group(w2s, self.act_s, self.ys, max_blocks=-(-T // bn),
                                          row_limit=T, flags=ops.GEMM_OUT_F32 | mf | wss))
@@ -97,8 +106,8 @@ class BlockChain:
             ops.grouped_gemm(w2_groups(False), H, I, ops.FUS_EPI_BF16, bn)
 
         def merge_step():
-            ops.merge(self.y.view(T, K, H), o.topw, o.h1, self.ys if self.shared else None,
-                      o.out, round_mid=False)
+            ops.merge_pos(self.xs, self.pos_of, K, o.topw, o.h1,
+                          self.ys if self.shared else None, o.out)
 
         if self.small:
             front = [("route_small", lambda: ops.route_small(
@@ -113,8 +122,8 @@ class BlockChain:
                                                         o.topw, o.topi)),
                 ("moe_align", lambda: ops.moe_align(o.topi, E, bn, self.sorted, self.eids,
                                                     self.ntp, self.align_ws)),
-                ("permute", lambda: ops.permute_rows(self.x2, self.sorted, self.ntp, K, self.R,
-                                                     self.xs, self.cap)),
+                ("permute", lambda: ops.permute_rows_pos(self.x2, self.sorted, self.ntp, K, self.R,
+                                                         self.xs, self.pos_of, self.cap)),
             ]
         if self.small:
             return front + [("w13_swiglu", w13_step), ("w2_merge", w2_merge_step)]

@@ -190,13 +190,14 @@ __global__ void align_scatter_kernel(const int* __restrict__ ids, int numel, int
 __global__ void permute_rows_kernel(const __nv_bfloat16* __restrict__ src, long ld_src,
                                     const int* __restrict__ sorted_ids, const int* __restrict__ ntp,
                                     int div, int num_valid, __nv_bfloat16* __restrict__ dst,
-                                    long ld_dst, int max_rows, int H) {
+                                    long ld_dst, int max_rows, int H, int* __restrict__ pos_of) {
   const int rows = min(__ldg(ntp), max_rows);
   const int warps = gridDim.x * (blockDim.x >> 5);
   const int nv = H >> 3;
   for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < rows; p += warps) {
     const int id = __ldg(sorted_ids + p);
     if (id >= num_valid) continue;  // dispatch pad: never multiplied, left as is
+    if (pos_of && (threadIdx.x & 31) == 0) pos_of[id] = p;
     uint4* d = reinterpret_cast<uint4*>(dst + (long)p * ld_dst);
     const uint4* s = reinterpret_cast<const uint4*>(src + (long)(id / div) * ld_src);
     for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = __ldg(s + v);
@@ -260,9 +261,9 @@ extern "C" int fus_moe_align(const int* ids, int numel, int E, int block_m, int*
   return check_launch("moe_align");
 }
 
-extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
-                                int div, int num_valid, void* dst, long ld_dst, int max_rows, int H,
-                                void* stream, int* status) {
+extern "C" int fus_permute_rows_pos(const void* src, long ld_src, const int* sorted_ids,
+                                    const int* ntp, int div, int num_valid, void* dst, long ld_dst,
+                                    int max_rows, int H, int* pos_of, void* stream, int* status) {
   (void)status;
   if (!src || !sorted_ids || !ntp || !dst || div < 1 || H <= 0 || H % 8 || max_rows < 0 ||
       !aligned16(src) || !aligned16(dst) || ld_src % 8 || ld_dst % 8)
@@ -273,8 +274,15 @@ extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_
   if (grid > cap) grid = cap;
   permute_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(
       (const __nv_bfloat16*)src, ld_src, sorted_ids, ntp, div, num_valid, (__nv_bfloat16*)dst,
-      ld_dst, max_rows, H);
+      ld_dst, max_rows, H, pos_of);
   return check_launch("permute_rows");
+}
+
+extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
+                                int div, int num_valid, void* dst, long ld_dst, int max_rows, int H,
+                                void* stream, int* status) {
+  return fus_permute_rows_pos(src, ld_src, sorted_ids, ntp, div, num_valid, dst, ld_dst, max_rows,
+                              H, nullptr, stream, status);
 }
 
 // ---- variant that allocates nothing ---------------------------------------------------

@@ -70,6 +70,26 @@ int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t
   return FUS_OK;
 }
 
+int make_tmap_store_2d(CUtensorMap* m, const void* base, bool f32, uint64_t inner, uint64_t rows,
+                       uint64_t ld, uint32_t box_inner, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(FUS_E_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  const uint64_t es = f32 ? 4 : 2;
+  if (!aligned16(base) || (ld * es) % 16 || (box_inner * es) % 16)
+    return set_error(FUS_E_INVALID, "store tensor map: base, pitch and box must be 16-byte aligned");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld * es};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FUS_E_INVALID, "cuTensorMapEncodeTiled (store) failed (%d)", (int)r);
+  return FUS_OK;
+}
+
 }  // namespace fus
 
 extern "C" int fus_version(void) { return 1; }

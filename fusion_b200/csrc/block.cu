@@ -33,10 +33,16 @@ struct BlockLayout {
   int R, cap, blocks_cap, max_blocks, nsplit;
   int tiles;
   size_t off_x2, off_partial, off_sorted, off_eids, off_ntp, off_align, off_xs, off_act, off_acts,
-      off_y, off_ys, off_cnt, off_done, total;
+      off_y, off_ys, off_cnt, off_done, off_pos, total;
 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// decode path: the fused front end (fus_moe_route_small) and gathered-row GEMMs
+bool small_path(const fus_moe_block_desc* d, int T) {
+  const int E = d->E, K = d->topk;
+  return T <= 16 && E <= 256 && E % 2 == 0 && T * K <= 256 && (d->nplanes == 1 || d->nplanes == 3);
+}
 
 bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   if (!d || T < 1 || bn < 16) return false;
@@ -63,10 +69,15 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   L.off_eids = take((size_t)L.blocks_cap * 4);
   L.off_ntp = take(16);
   L.off_align = take(fus_moe_align_workspace(L.R, E));
-  L.off_xs = T <= 16 ? 0 : take((size_t)L.cap * H * 2);  // permuted rows (prefill only)
+  const bool small = small_path(d, T);
+  L.off_xs = small ? 0 : take((size_t)L.cap * H * 2);  // permuted rows (prefill only)
   L.off_act = take((size_t)L.cap * I * 2);
   L.off_acts = take((size_t)T * I * 2);
-  L.off_y = take((size_t)L.R * H * 2);
+  // decode: y[pair] in pair order (fused merge); prefill: the down projection's rows in
+  // dispatch order, in the permuted-row buffer (dead once w13 has read it), gathered back
+  // per token through pos_of by the merge
+  L.off_y = small ? take((size_t)L.R * H * 2) : L.off_xs;
+  L.off_pos = small ? 0 : take((size_t)L.R * 4);
   L.off_ys = take((size_t)T * H * 4);  // shared expert output, fp32
   L.tiles = fus_grouped_gemm_tiles(H, FUS_EPI_BF16, bn);
   L.off_cnt = take((size_t)T * L.tiles * 4);  // fused-merge arrival counters
@@ -130,11 +141,11 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   void* ys = at(L.off_ys);
   int* counters = reinterpret_cast<int*>(at(L.off_cnt));
   int* done = reinterpret_cast<int*>(at(L.off_done));
+  int* pos_of = reinterpret_cast<int*>(at(L.off_pos));
   const bool shared = d->w13s != nullptr;
 
   int rc;
-  const bool small = T <= 16 && E <= 256 && E % 2 == 0 && T * K <= 256 &&
-                     (d->nplanes == 1 || d->nplanes == 3);
+  const bool small = small_path(d, T);
   if (small) {
     // decode: norm + router + top-k + layout in one launch; it also clears the merge
     // counters, so the down projection needs no separate reset
@@ -156,7 +167,8 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
     if ((rc = fus_moe_align(topi, L.R, E, block_n, sorted, L.cap, eids, L.blocks_cap, ntp,
                             align_ws, fus_moe_align_workspace(L.R, E), stream, status)))
       return rc;
-    if ((rc = fus_permute_rows(x2, H, sorted, ntp, K, L.R, xs, H, L.cap, H, stream, status)))
+    if ((rc = fus_permute_rows_pos(x2, H, sorted, ntp, K, L.R, xs, H, L.cap, H, pos_of, stream,
+                                   status)))
       return rc;
   }
 
@@ -223,13 +235,16 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   g[1].flags = FUS_GEMM_OUT_F32 | (T <= block_n ? FUS_GEMM_W_STREAM : 0);
   g[1].token_div = 1;
   if (!small) {
-    // prefill: the merge is a bandwidth-bound pass of its own (in GEMM epilogues it
-    // would be serialised behind each CTA's MMAs)
+    // prefill: rows land in dispatch order (dense tile stores, no scatter); the merge is
+    // a bandwidth-bound pass of its own (in GEMM epilogues it would be serialised behind
+    // each CTA's MMAs)
+    g[0].row_map = nullptr;
+    g[0].row_limit = L.cap;
     if ((rc = fus_grouped_gemm(g, shared ? 2 : 1, H, I, 1, FUS_EPI_BF16, block_n, 1, 0, stream,
                                status)))
       return rc;
-    return fus_merge(y, (long)K * H, H, K, topw, K, h1, H, shared ? ys : nullptr, H, 1, out, H, T,
-                     H, /*round_mid=*/0, stream, status);
+    return fus_merge_pos(y, H, pos_of, K, topw, K, h1, H, shared ? ys : nullptr, H, 1, out, H, T,
+                         H, stream, status);
   }
   // decode: the CTA that lands the last contribution of a (token, tile) writes
   // out = bf16(sum_k w_k y_k + h1 + ys) for it (counters cleared by the front end)

@@ -171,6 +171,36 @@ FUS_DEVICE uint64_t policy_evict_last() {
   return p;
 }
 // 2D tile load; c0 = inner (contiguous) coordinate in elements, c1 = row.
+// SwiGLU of one fp32 gate/up pair in the GEMM epilogues: silu(g) * up with the fast
+// exponential and division intrinsics (a few ulp from the IEEE expression, far inside the
+// block's tolerance; the accumulators themselves are not exact to that level anyway)
+FUS_DEVICE float silu_mul(float g, float up) { return __fdividef(g, 1.0f + __expf(-g)) * up; }
+
+// ---- TMA tile store from shared memory (bulk-group completion) ----
+// generic-proxy writes to the source tile must be fenced (fence_proxy_async_smem) and
+// made CTA-visible (a barrier) before one thread issues the store
+FUS_DEVICE void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+FUS_DEVICE void tma_store_2d(const CUtensorMap* m, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+FUS_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of all committed stores have been read (may be reused)
+FUS_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// all committed stores are complete in global memory
+FUS_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// 16-byte global store with an L2 eviction-policy hint
+FUS_DEVICE void st_global_v4_hint(void* p, uint4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w), "l"(policy)
+               : "memory");
+}
+
 FUS_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1,
                             uint64_t policy) {
   asm volatile(
@@ -230,6 +260,26 @@ FUS_DEVICE void tc_commit(uint32_t bar) {
       : "memory");
 }
 // 32 lanes x 32 bit, 16 consecutive columns per thread
+// tcgen05.ld of 16 columns without the wait; tmem_ld_wait(r) completes it (its operands
+// tie the registers to the wait so no use is scheduled before it)
+FUS_DEVICE void tmem_ld16_issue(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+FUS_DEVICE void tmem_ld_wait(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 FUS_DEVICE void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(

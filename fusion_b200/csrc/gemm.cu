@@ -39,6 +39,7 @@ struct GroupDev {
   int token_div;
   const int* gather_ids;
   int gather_div;
+  int tma_store;  // persistent kernel: dense output written by TMA tile stores
 };
 
 struct MergeDev {
@@ -390,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 16; ++j) {
               const float g = exact ? v[j] : round_bf(v[j]);
               const float up = exact ? w[j] : round_bf(w[j]);
-              v[j] = (g / (1.0f + expf(-g))) * up;
+              v[j] = silu_mul(g, up);
             }
           } else {
             tmem_ld16(lane_base + (uint32_t)(pass * BN + c), v);
@@ -423,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + expf(-g[e]))) * uu[e];
+            for (int e = 0; e < 8; ++e) o[e] = silu_mul(g[e], uu[e]);
             *reinterpret_cast<uint4*>(out + (long)row * G.ldo + mt * 64 + q * 8) = pack8(o);
           }
         } else {
@@ -497,8 +498,8 @@ int launch_p(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t 
   });
   if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
                                                 cudaGetErrorString(attr_err));
-  grouped_gemm_persistent<BN, EPI><<<grid, kPThreads, Cfg::SMEM_BYTES, st>>>(maps[0], maps[1],
-                                                                          maps[2], maps[3], a);
+  grouped_gemm_persistent<BN, EPI><<<grid, kPThreads, Cfg::SMEM_BYTES, st>>>(
+      maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[4], maps[5], a);
   return check_launch("grouped_gemm_persistent");
 }
 
@@ -682,7 +683,7 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
   }
   a.group_blocks = group_blocks;
 
-  CUtensorMap maps[4];
+  CUtensorMap maps[10] = {};
   long units[2] = {0, 0};
   const int a_box_rows = (epilogue == FUS_EPI_SWIGLU && !mt2) ? 64 : 128;
   const int out_cols = epilogue == FUS_EPI_SWIGLU ? w_rows / 2 : w_rows;
@@ -743,6 +744,32 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
       !(groups[0].flags & FUS_GEMM_NO_PERSIST) && !groups[0].gather_ids &&
       (ngroups < 2 || !groups[1].gather_ids)) {
     const int grid = (int)(total < sms ? total : sms);
+    for (int g = 0; g < ngroups; ++g) {
+      const fus_gemm_group& G = groups[g];
+      a.g[g].tma_store = 0;
+      if (G.row_map || G.row_scale || G.row_limit < 1) continue;
+      const bool out32 = epilogue == FUS_EPI_BF16 && (G.flags & FUS_GEMM_OUT_F32);
+      // one store = half a staging buffer: 128 features x (32 bf16 | 16 fp32) token rows
+      int rc = make_tmap_store_2d(&maps[4 + g], G.out, out32, (uint64_t)out_cols,
+                                  (uint64_t)G.row_limit, (uint64_t)G.ldo, 128, out32 ? 16 : 32);
+      if (rc) return rc;
+      a.g[g].tma_store = 1;
+    }
+    if (ngroups == 1) maps[5] = maps[4];
+    // token maps with 32- and 128-row boxes for blocks with few live rows
+    for (int g = 0; g < ngroups; ++g) {
+      const fus_gemm_group& G = groups[g];
+      int rc = make_tmap_bf16_2d(&maps[6 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
+                                 (uint64_t)G.ldx, kBK, 32);
+      if (!rc)
+        rc = make_tmap_bf16_2d(&maps[8 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
+                               (uint64_t)G.ldx, kBK, block_n < 128 ? block_n : 128);
+      if (rc) return rc;
+    }
+    if (ngroups == 1) {
+      maps[7] = maps[6];
+      maps[9] = maps[8];
+    }
     return epilogue == FUS_EPI_SWIGLU ? launch_persist<FUS_EPI_SWIGLU>(block_n, maps, a, grid, st)
                                       : launch_persist<FUS_EPI_BF16>(block_n, maps, a, grid, st);
   }

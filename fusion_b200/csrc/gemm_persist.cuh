@@ -82,6 +82,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
                             const __grid_constant__ CUtensorMap ta1,
                             const __grid_constant__ CUtensorMap tb0,
                             const __grid_constant__ CUtensorMap tb1,
+                            const __grid_constant__ CUtensorMap tbs0,  // token box 32 rows
+                            const __grid_constant__ CUtensorMap tbs1,
+                            const __grid_constant__ CUtensorMap tbm0,  // token box 128 rows
+                            const __grid_constant__ CUtensorMap tbm1,
+                            const __grid_constant__ CUtensorMap to0,
+                            const __grid_constant__ CUtensorMap to1,
                             const __grid_constant__ GemmArgs args) {
   using Cfg = PersistCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -130,17 +136,27 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer: one continuous ring over all units ----------------
-      const uint64_t pol_x = policy_evict_last();
-      uint32_t c = 0;
-      bool stop = false;
-      for (long uu = blockIdx.x; uu < total && !stop; uu += gridDim.x) {
-        Unit un;
-        if (!decode_unit(args, (int)uu, BN, un, true)) continue;
-        const GroupDev& G = args.g[un.gi];
+    // ---------------- TMA producer: one continuous ring over all units ----------------
+    // The token box is sized to the block's live rows (32 / 128 / BN): a block that holds
+    // the few tokens an expert has beyond a full block moves 4 KB of tokens per stage,
+    // not 32 KB of mostly dispatch pads.
+    const uint64_t pol_x = policy_evict_last();
+    uint32_t c = 0;
+    bool stop = false;
+    for (long uu = blockIdx.x; uu < total && !stop; uu += gridDim.x) {
+      Unit un;
+      if (!decode_unit(args, (int)uu, BN, un, lane == 0)) continue;
+      const GroupDev& G = args.g[un.gi];
+      const int pos0 = un.blk * BN;
+      const int n_live = live_columns(G, pos0, BN, lane);
+      if (lane == 0) {
         const CUtensorMap* tma_a = un.gi ? &ta1 : &ta0;
-        const CUtensorMap* tma_b = un.gi ? &tb1 : &tb0;
+        constexpr int kMid = BN < 128 ? BN : 128;  // the tbm maps' box rows
+        const int bx = n_live <= 32 ? 32 : (n_live <= kMid ? kMid : BN);
+        const CUtensorMap* tma_b = bx == 32    ? (un.gi ? &tbs1 : &tbs0)
+                                   : bx == kMid ? (un.gi ? &tbm1 : &tbm0)
+                                                : (un.gi ? &tb1 : &tb0);
+        const uint32_t stage_bytes = Cfg::A_BYTES + (uint32_t)bx * kBK * 2;
         const uint64_t pol_w = (G.flags & FUS_GEMM_W_STREAM) ? policy_evict_first()
                                                              : policy_evict_normal();
         const int ebase = un.expert * args.w_rows;
@@ -152,7 +168,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
           a_row0 = ebase + un.mt * 256;
           a_row1 = a_row0 + 128;
         }
-        const int pos0 = un.blk * BN;
         for (int i = 0; i < nk; ++i, ++c) {
           const int s = c % STAGES;
           const uint32_t r = c / STAGES;
@@ -162,13 +177,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
           }
           const uint32_t full = bar_full + 8 * s;
           const int kk = i * kBK;
-          mbar_arrive_expect_tx(full, Cfg::STAGE_BYTES);
+          mbar_arrive_expect_tx(full, stage_bytes);
           const uint32_t a_dst = sA + s * Cfg::A_BYTES;
           tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
           tma_load_2d(a_dst + kATileBytes, tma_a, full, kk, a_row1, pol_w);
           tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, pos0, pol_x);
         }
       }
+      stop = __shfl_sync(0xffffffffu, (int)stop, 0);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -225,7 +241,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int bar_id = 1 + eg;
     uint8_t* staging = staging_all + eg * Cfg::STAGING_BYTES;
     volatile int* my_ok = ep_ok + eg;
-    uint32_t t = 0;
+    // outputs are streamed: keep them from evicting the weight and token tiles that
+    // neighbouring units re-read from L2
+    const uint64_t pol_out = policy_evict_first();
+    uint32_t t = 0, half = 0;
     for (long uu = blockIdx.x; uu < total; uu += gridDim.x) {
       Unit un;
       if (!decode_unit(args, (int)uu, BN, un, false)) continue;
@@ -236,73 +255,155 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const uint32_t buf = t % Cfg::NBUF, use = t / Cfg::NBUF;
       const uint32_t lane_base =
           tmem + buf * Cfg::ACC_COLS + ((uint32_t)(q4 * 32) << 16);
+      const bool exact = G.flags & FUS_GEMM_SWIGLU_EXACT;
+      const bool out32 = (EPI == FUS_EPI_BF16) && (G.flags & FUS_GEMM_OUT_F32);
+      // dense outputs (no row map / scale) leave through TMA tile stores from alternating
+      // 8 KB halves of the group's staging buffer (one store drains while the next half
+      // fills); scattered rows go through 16-byte stores from the whole 16 KB
+      const bool tma_out = G.tma_store;
+      const CUtensorMap* tmo = un.gi ? &to1 : &to0;
+      const int CH = tma_out ? (out32 ? 16 : 32) : (out32 ? 32 : 64);  // tokens per round
+      const int vec_per_row = out32 ? 32 : 16;  // 16-byte vectors per 128 features
+      // each group drains one pass: with two passes (bf16/fp32 output) group g takes pass
+      // g, with SwiGLU the groups take alternate token chunks
+      constexpr int PASSES = (EPI == FUS_EPI_SWIGLU) ? 1 : 2;
+      const int pass = PASSES == 2 ? eg : 0;
+      const int c_first = PASSES == 2 ? 0 : eg * CH;
+      const int c_step = PASSES == 2 ? CH : kPEpiGroups * CH;
+      // destination rows of a chunk: store k of this thread is 16-byte vector et + 128 k
+      // (CH * vec_per_row / 128 = 8 stores per thread and chunk); -1 = no store. The rows
+      // of the first chunk are fetched before the accumulator wait and each next chunk's
+      // during the current one, so the index loads never stall the drain.
+      auto fetch_rows = [&](int c0, int* rr) {
+        const int nrow = min(min(CH, n_mma - c0), n_live - c0);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int j = (et + 128 * k) / vec_per_row;
+          int row = -1;
+          if (j < nrow) {
+            const int pos = pos0 + c0 + j;
+            row = G.row_map ? __ldg(G.row_map + pos) : pos;
+            if (row >= G.row_limit) row = -1;
+          }
+          rr[k] = row;
+        }
+      };
+      int rr[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+      if (!tma_out) fetch_rows(c_first, rr);
       if (et == 0)
         *my_ok = mbar_wait_bounded(bar_acc_full + 8 * buf, use & 1u, abort_flag, args.status);
       named_bar_sync(bar_id, 128);
       if (!*my_ok) break;
       tc_fence_after();
-      const bool exact = G.flags & FUS_GEMM_SWIGLU_EXACT;
-      const bool out32 = (EPI == FUS_EPI_BF16) && (G.flags & FUS_GEMM_OUT_F32);
-      const int CH = out32 ? 32 : 64;  // tokens per staging round (16 KB)
-      constexpr int PASSES = (EPI == FUS_EPI_SWIGLU) ? 1 : 2;
-      for (int pass = (PASSES == 2 ? eg : 0); pass < PASSES; pass += kPEpiGroups) {
+      {
         const int col0 = (EPI == FUS_EPI_SWIGLU) ? un.mt * 128 : (un.mt * 2 + pass) * 128;
-        const int c_first = PASSES == 2 ? 0 : eg * CH;
-        const int c_step = PASSES == 2 ? CH : kPEpiGroups * CH;
         for (int c0 = c_first; c0 < n_mma; c0 += c_step) {
           const int cw = min(CH, n_mma - c0);
-          for (int c = 0; c < cw; c += 16) {
-            float v[16];
-            if (EPI == FUS_EPI_SWIGLU) {
-              float u[16];
-              tmem_ld16(lane_base + (uint32_t)(c0 + c), v);
-              tmem_ld16(lane_base + (uint32_t)(BN + c0 + c), u);
+          uint8_t* stg = tma_out ? staging + (half & 1u) * (Cfg::STAGING_BYTES / 2) : staging;
+          int rn[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+          if (!tma_out && c0 + c_step < n_mma) fetch_rows(c0 + c_step, rn);
+          // one staging column group: scale (w2 with row_scale), convert, write to smem
+          auto stage16 = [&](int c, float* v) {
+            if (EPI != FUS_EPI_SWIGLU && G.row_scale) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                const float g = exact ? v[j] : round_bf(v[j]);
-                const float up = exact ? u[j] : round_bf(u[j]);
-                v[j] = (g / (1.0f + expf(-g))) * up;
-              }
-            } else {
-              tmem_ld16(lane_base + (uint32_t)(pass * BN + c0 + c), v);
-              if (G.row_scale) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const int pos = pos0 + c0 + c + j;
-                  const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
-                  v[j] *= row < G.row_limit ? __ldg(G.row_scale + row) : 0.f;
-                }
+                const int pos = pos0 + c0 + c + j;
+                const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
+                v[j] *= row < G.row_limit ? __ldg(G.row_scale + row) : 0.f;
               }
             }
             if (out32) {
-              float* st = reinterpret_cast<float*>(staging);
+              float* st = reinterpret_cast<float*>(stg);
 #pragma unroll
               for (int j = 0; j < 16; ++j) st[(c + j) * 128 + m] = v[j];
             } else {
-              __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
+              __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg);
 #pragma unroll
               for (int j = 0; j < 16; ++j) st[(c + j) * 128 + m] = __float2bfloat16_rn(v[j]);
             }
+          };
+          auto swiglu16 = [&](const uint32_t* rg, const uint32_t* ru, float* v) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float g0 = __uint_as_float(rg[j]), u0 = __uint_as_float(ru[j]);
+              const float g = exact ? g0 : round_bf(g0);
+              const float up = exact ? u0 : round_bf(u0);
+              v[j] = silu_mul(g, up);
+            }
+          };
+          // TMEM reads in batches of 32 token columns, one wait per batch
+          for (int c = 0; c < cw; c += 32) {
+            const bool two = c + 16 < cw;  // warp-uniform
+            uint32_t ra[16], rb[16], rc[16], rd[16];
+            float v[16];
+            if (EPI == FUS_EPI_SWIGLU) {
+              tmem_ld16_issue(lane_base + (uint32_t)(c0 + c), ra);
+              tmem_ld16_issue(lane_base + (uint32_t)(BN + c0 + c), rb);
+              if (two) {
+                tmem_ld16_issue(lane_base + (uint32_t)(c0 + c + 16), rc);
+                tmem_ld16_issue(lane_base + (uint32_t)(BN + c0 + c + 16), rd);
+              }
+              tmem_ld_wait(ra);
+              tmem_ld_wait(rb);
+              if (two) {
+                tmem_ld_wait(rc);
+                tmem_ld_wait(rd);
+              }
+              swiglu16(ra, rb, v);
+              stage16(c, v);
+              if (two) {
+                swiglu16(rc, rd, v);
+                stage16(c + 16, v);
+              }
+            } else {
+              tmem_ld16_issue(lane_base + (uint32_t)(pass * BN + c0 + c), ra);
+              if (two) tmem_ld16_issue(lane_base + (uint32_t)(pass * BN + c0 + c + 16), rc);
+              tmem_ld_wait(ra);
+              if (two) tmem_ld_wait(rc);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(ra[j]);
+              stage16(c, v);
+              if (two) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(rc[j]);
+                stage16(c + 16, v);
+              }
+            }
+          }
+          if (tma_out) {
+            // the previous store (other half) must have read its source before anyone
+            // passes this barrier into the next chunk, which refills that half. Rows past
+            // the map's extent (row_limit) are clipped by the copy engine; rows past n_live
+            // inside the block are dispatch pads (their contents are unused).
+            fence_proxy_async_smem();
+            if (et == 0) bulk_wait_read_all();
+            named_bar_sync(bar_id, 128);
+            if (et == 0) {
+              tma_store_2d(tmo, smem_u32(stg), col0, pos0 + c0);
+              bulk_commit();
+            }
+            ++half;
+            continue;
           }
           named_bar_sync(bar_id, 128);
-          const int nrow = min(cw, n_live - c0);
-          const int vec_per_row = out32 ? 32 : 16;  // 16-byte vectors per 128 features
-          for (int it = et; it < nrow * vec_per_row; it += 128) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            if (rr[k] < 0) continue;
+            const int it = et + 128 * k;
             const int j = it / vec_per_row, q = it % vec_per_row;
-            const int pos = pos0 + c0 + j;
-            const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
-            if (row >= G.row_limit) continue;
             if (out32) {
               const uint4 val = reinterpret_cast<const uint4*>(staging)[j * 32 + q];
-              *reinterpret_cast<uint4*>(reinterpret_cast<float*>(G.out) + (long)row * G.ldo +
-                                        col0 + q * 4) = val;
+              st_global_v4_hint(reinterpret_cast<float*>(G.out) + (long)rr[k] * G.ldo + col0 +
+                                    q * 4, val, pol_out);
             } else {
               const uint4 val = reinterpret_cast<const uint4*>(staging)[j * 16 + q];
-              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(G.out) +
-                                        (long)row * G.ldo + col0 + q * 8) = val;
+              st_global_v4_hint(reinterpret_cast<__nv_bfloat16*>(G.out) + (long)rr[k] * G.ldo +
+                                    col0 + q * 8, val, pol_out);
             }
           }
           named_bar_sync(bar_id, 128);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) rr[k] = rn[k];
         }
       }
       // accumulators read: hand TMEM back to the MMA warp for the next unit
@@ -311,6 +412,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (et == 0) mbar_arrive(bar_acc_empty + 8 * buf);
       ++t;
     }
+    if (et == 0) bulk_wait_all();  // stores complete before the CTA's shared memory goes
   }
 
   tc_fence_before();

@@ -19,6 +19,9 @@ int check_launch(const char* what);
 // row, `rows` rows, row pitch `ld` elements, box = box_inner x box_rows.
 int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t ld,
                       uint32_t box_inner, uint32_t box_rows);
+// row-major output tile map for TMA stores (no swizzle: the staging tile is row-major)
+int make_tmap_store_2d(CUtensorMap* m, const void* base, bool f32, uint64_t inner, uint64_t rows,
+                       uint64_t ld, uint32_t box_inner, uint32_t box_rows);
 int num_sms();
 
 // Grouped GEMM entry used inside the library with programmatic dependent launch:

@@ -92,7 +92,7 @@ __global__ void silu_and_mul_kernel(const __nv_bfloat16* __restrict__ x, long ld
 // ======================================================================================
 template <int KT>
 __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, long ld_k, int K,
-                             const float* __restrict__ w, long ldw,
+                             const int* __restrict__ pos_of, const float* __restrict__ w, long ldw,
                              const __nv_bfloat16* __restrict__ res, long ldr,
                              const void* __restrict__ extra, long lde, int extra_f32,
                              __nv_bfloat16* __restrict__ out, long ldo, int H, int round_mid) {
@@ -103,11 +103,16 @@ __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, lon
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  // row of (t, k): y + t*ld_t + k*ld_k, or y + pos_of[t*K + k]*ld_k (rows stored in
+  // dispatch order)
   const __nv_bfloat16* yt = y + (long)t * ld_t + c;
+  auto yrow = [&](int k) {
+    return pos_of ? y + (long)__ldg(pos_of + (long)t * nk + k) * ld_k + c : yt + (long)k * ld_k;
+  };
   if (KT > 0) {
     uint4 yv[KT > 0 ? KT : 1];
 #pragma unroll
-    for (int k = 0; k < (KT > 0 ? KT : 1); ++k) yv[k] = ldg_stream(yt + (long)k * ld_k);
+    for (int k = 0; k < (KT > 0 ? KT : 1); ++k) yv[k] = ldg_stream(yrow(k));
 #pragma unroll
     for (int k = 0; k < (KT > 0 ? KT : 1); ++k) {
       const float wk = w ? __ldg(w + (long)t * ldw + k) : 1.0f;
@@ -120,7 +125,7 @@ __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, lon
     for (int k = 0; k < nk; ++k) {
       const float wk = w ? __ldg(w + (long)t * ldw + k) : 1.0f;
       float f[8];
-      unpack8(ldg_stream(yt + (long)k * ld_k), f);
+      unpack8(ldg_stream(yrow(k)), f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] += wk * f[e];
     }
@@ -225,11 +230,10 @@ extern "C" int fus_silu_and_mul(const void* x, long ldx, void* y, long ldy, int 
   return check_launch("silu_and_mul");
 }
 
-extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long ldw,
-                         const void* res, long ldr, const void* extra, long lde, int extra_f32,
-                         void* out, long ldo, int T, int H, int round_mid, void* stream,
-                         int* status) {
-  (void)status;
+static int merge_launch(const void* y, long ld_t, long ld_k, int K, const int* pos_of,
+                        const float* w, long ldw, const void* res, long ldr, const void* extra,
+                        long lde, int extra_f32, void* out, long ldo, int T, int H, int round_mid,
+                        void* stream) {
   if (T < 0 || H <= 0 || H % 8 || K < 0) return set_error(FUS_E_INVALID, "merge: bad shape");
   if (K > 0 && (!y || !aligned16(y) || ld_t % 8 || ld_k % 8))
     return set_error(FUS_E_INVALID, "merge: y rows must be 16-byte aligned");
@@ -240,14 +244,33 @@ extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float
   cudaStream_t st = as_stream(stream);
   dim3 grid = row_grid(T, H, 128);
   if (K == 8)
-    merge_kernel<8><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, w, ldw, (const bf16*)res,
+    merge_kernel<8><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, pos_of, w, ldw, (const bf16*)res,
                                           ldr, extra, lde, extra_f32, (bf16*)out, ldo, H,
                                           round_mid);
   else
-    merge_kernel<0><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, w, ldw, (const bf16*)res,
+    merge_kernel<0><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, pos_of, w, ldw, (const bf16*)res,
                                           ldr, extra, lde, extra_f32, (bf16*)out, ldo, H,
                                           round_mid);
   return check_launch("merge");
+}
+
+extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long ldw,
+                         const void* res, long ldr, const void* extra, long lde, int extra_f32,
+                         void* out, long ldo, int T, int H, int round_mid, void* stream,
+                         int* status) {
+  (void)status;
+  return merge_launch(y, ld_t, ld_k, K, nullptr, w, ldw, res, ldr, extra, lde, extra_f32, out, ldo,
+                      T, H, round_mid, stream);
+}
+
+extern "C" int fus_merge_pos(const void* y, long ldy, const int* pos_of, int K, const float* w,
+                             long ldw, const void* res, long ldr, const void* extra, long lde,
+                             int extra_f32, void* out, long ldo, int T, int H, void* stream,
+                             int* status) {
+  (void)status;
+  if (K > 0 && !pos_of) return set_error(FUS_E_INVALID, "merge_pos: pos_of is NULL");
+  return merge_launch(y, 0, ldy, K, pos_of, w, ldw, res, ldr, extra, lde, extra_f32, out, ldo, T,
+                      H, 0, stream);
 }
 
 extern "C" int fus_add(const void* a, long lda, const void* b, long ldb, void* o, long ldo, int M,

@@ -144,6 +144,16 @@ def permute_rows(src, sorted_ids, ntp, div: int, num_valid: int, dst, max_rows: 
            _ld(dst), max_rows, H, _stream(), _sp())
 
 
+def permute_rows_pos(src, sorted_ids, ntp, div: int, num_valid: int, dst, pos_of,
+                     max_rows: int | None = None):
+    """permute_rows that also records pos_of[sorted_ids[p]] = p for the live positions."""
+    H = src.shape[1]
+    if max_rows is None:
+        max_rows = min(dst.shape[0], sorted_ids.numel())
+    L.call("fus_permute_rows_pos", _p(src), _ld(src), _p(sorted_ids), _p(ntp), div, num_valid,
+           _p(dst), _ld(dst), max_rows, H, _p(pos_of), _stream(), _sp())
+
+
 def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map=None,
                row_limit: int, row_scale=None, x_rows: int | None = None,
                flags: int = 0, live_ids=None, live_limit: int = 0,
@@ -223,6 +233,16 @@ def merge(y3, w, res, extra, out, round_mid: bool = True):
            _p(extra), _ld(extra) if extra is not None else 0,
            int(extra is not None and extra.dtype == torch.float32), _p(out), _ld(out), T, H,
            int(round_mid), _stream(), _sp())
+
+
+def merge_pos(y, pos_of, K: int, w, res, extra, out):
+    """merge over rows in dispatch order: row (t, k) = y[pos_of[t*K + k]] (y: [rows, H])."""
+    T, H = out.shape
+    L.call("fus_merge_pos", _p(y), _ld(y), _p(pos_of), K, _p(w),
+           w.stride(0) if w is not None else 0, _p(res), _ld(res) if res is not None else 0,
+           _p(extra), _ld(extra) if extra is not None else 0,
+           int(extra is not None and extra.dtype == torch.float32), _p(out), _ld(out), T, H,
+           _stream(), _sp())
 
 
 def add(a, b, o):

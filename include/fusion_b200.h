@@ -158,6 +158,12 @@ int fus_moe_route_small(const void* h, const void* r, const void* gamma, float e
 int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp, int div,
                      int num_valid, void* dst, long ld_dst, int max_rows, int H, void* stream,
                      int* status);
+/* Same, and records where each pair landed: pos_of[sorted_ids[p]] = p for the live
+ * positions p (pos_of has num_valid entries). With the down projection's rows stored in
+ * dispatch order, fus_merge_pos gathers them back per token through pos_of. */
+int fus_permute_rows_pos(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
+                         int div, int num_valid, void* dst, long ld_dst, int max_rows, int H,
+                         int* pos_of, void* stream, int* status);
 
 /* ---------------------------------------------------------------------------------
  * Grouped expert GEMM on tcgen05 tensor cores (replaces the Triton grouped GEMMs
@@ -198,8 +204,9 @@ typedef struct fus_gemm_group {
   int flags;              /* FUS_GEMM_* bits                                               */
   const int* live_ids;    /* optional: column j of block b is live iff                     */
   int live_limit;         /*   live_ids[b*block_n + j] < live_limit; dead columns sit at   */
-                          /*   the end of a block (dispatch pads) and are neither          */
-                          /*   multiplied (the MMA N shrinks) nor written                  */
+                          /*   the end of a block (dispatch pads) and are not multiplied   */
+                          /*   (the MMA N shrinks); with row_map NULL their output rows    */
+                          /*   (< row_limit) may receive unspecified values                */
   int token_div;          /* FUS_GEMM_MERGE: token of output row r is r / token_div        */
   const int* gather_ids;  /* optional: token rows are gathered, not read densely: row j of */
   int gather_div;         /*   block b is x[gather_ids[b*block_n+j] / gather_div] when that */
@@ -264,6 +271,11 @@ int fus_silu_and_mul(const void* x, long ldx, void* y, long ldy, int M, int I, v
 int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long ldw,
               const void* res, long ldr, const void* extra, long lde, int extra_f32, void* out,
               long ldo, int T, int H, int round_mid, void* stream, int* status);
+/* fus_merge over expert rows stored in dispatch order: row (t, k) is
+ * y + pos_of[t*K + k]*ldy (round_mid = 0). */
+int fus_merge_pos(const void* y, long ldy, const int* pos_of, int K, const float* w, long ldw,
+                  const void* res, long ldr, const void* extra, long lde, int extra_f32,
+                  void* out, long ldo, int T, int H, void* stream, int* status);
 
 /* moe_down_merge.py:532 launch_resadd / merge_resadd.py:253 resadd_only:
  *   o = bf16(a + b) */

@@ -97,11 +97,11 @@ SIGNATURES: dict[str, tuple] = {
     "fus_router_topk": (i32, [vp, i32, vp, vp, vp, vp, i32, i32, i32, f32, i32, vp, vp]),
     "fus_moe_align_workspace": (sz, [i32, i32]),
     "fus_moe_align": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, sz, vp, vp]),
+    "fus_moe_align_pos": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp, sz, vp, vp]),
     "fus_moe_align_noalloc": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp]),
     "fus_moe_route_small": (i32, [vp, vp, vp, f32, vp, i32, vp, i32, i32, i32, i32, f32, i32, vp, vp,
                                   vp, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, i32, vp, vp]),
     "fus_permute_rows": (i32, [vp, i64, vp, vp, i32, i32, vp, i64, i32, i32, vp, vp]),
-    "fus_permute_rows_pos": (i32, [vp, i64, vp, vp, i32, i32, vp, i64, i32, i32, vp, vp, vp]),
     "fus_merge_pos": (i32, [vp, i64, vp, i32, vp, i64, vp, i64, vp, i64, i32, vp, i64, i32, i32,
                             vp, vp]),
     "fus_grouped_gemm": (i32, [C.POINTER(GemmGroup), i32, i32, i32, i32, i32, i32, i32, i64, vp, vp]),

@@ -41,9 +41,9 @@ class BlockChain:
         self.xs = None if self.small else torch.empty(cap, H, dtype=bf, device=dev)
         self.act = torch.empty(cap, I, dtype=bf, device=dev)
         self.act_s = torch.empty(T, I, dtype=bf, device=dev)
-        # decode: y in pair order (fused merge); prefill: rows in dispatch order, stored
-        # over the permuted rows (dead after w13) and merged through pos_of
-        self.y = torch.empty(R, H, dtype=bf, device=dev) if self.small else None
+        # decode: y in pair order (fused merge); prefill: rows in dispatch order (dense
+        # tile stores) over the permuted rows (dead after w13), merged through pos_of
+        self.y = torch.empty(R, H, dtype=bf, device=dev) if self.small else self.xs
         self.pos_of = torch.empty(R, dtype=torch.int32, device=dev)
         self.ys = torch.empty(T, H, dtype=torch.float32, device=dev)
         self.tiles = ops.gemm_tiles(H, ops.FUS_EPI_BF16, bn)
@@ -87,7 +87,7 @@ class BlockChain:
                                     row_limit=self.R, flags=ws | mf, live_ids=self.sorted,
                                     live_limit=self.R, token_div=K)
             else:
-                g0 = ops.gemm_group(w2, self.act, self.xs, expert_ids=self.eids, ntp=self.ntp,
+                g0 = ops.gemm_group(w2, self.act, self.y, expert_ids=self.eids, ntp=self.ntp,
                                     max_blocks=self.max_blocks, row_limit=self.cap, flags=ws,
                                     live_ids=self.sorted, live_limit=self.R)
             gs = [g0]
@@ -106,7 +106,7 @@ class BlockChain:
             ops.grouped_gemm(w2_groups(False), H, I, ops.FUS_EPI_BF16, bn)
 
         def merge_step():
-            ops.merge_pos(self.xs, self.pos_of, K, o.topw, o.h1,
+            ops.merge_pos(self.y, self.pos_of, K, o.topw, o.h1,
                           self.ys if self.shared else None, o.out)
 
         if self.small:
@@ -121,9 +121,9 @@ class BlockChain:
                 ("router_topk", lambda: ops.router_topk(self.partial, self.nsplit, bias, None,
                                                         o.topw, o.topi)),
                 ("moe_align", lambda: ops.moe_align(o.topi, E, bn, self.sorted, self.eids,
-                                                    self.ntp, self.align_ws)),
-                ("permute", lambda: ops.permute_rows_pos(self.x2, self.sorted, self.ntp, K, self.R,
-                                                         self.xs, self.pos_of, self.cap)),
+                                                    self.ntp, self.align_ws, self.pos_of)),
+                ("permute", lambda: ops.permute_rows(self.x2, self.sorted, self.ntp, K, self.R,
+                                                     self.xs, self.cap)),
             ]
         if self.small:
             return front + [("w13_swiglu", w13_step), ("w2_merge", w2_merge_step)]

@@ -104,7 +104,8 @@ __device__ void place_experts(const int* cnt, int* start, int E, int block_m, in
 __global__ void __launch_bounds__(kAlignThreads)
     align_small_kernel(const int* __restrict__ ids, int numel, int E, int block_m,
                        int* __restrict__ sorted_ids, int sorted_cap, int* __restrict__ expert_ids,
-                       int blocks_cap, int* __restrict__ ntp, int* status) {
+                       int blocks_cap, int* __restrict__ ntp, int* __restrict__ pos_of,
+                       int* status) {
   extern __shared__ int sm[];
   int* wcnt = sm;                            // [32][E]
   int* cursor = wcnt + kAlignWarps * E;      // [E]
@@ -130,6 +131,7 @@ __global__ void __launch_bounds__(kAlignThreads)
     if (e < 0) continue;
     const int p = start[e] + rank[i];
     if (p < sorted_cap) sorted_ids[p] = i;
+    if (pos_of) pos_of[i] = p;
   }
 }
 
@@ -176,7 +178,8 @@ __global__ void __launch_bounds__(kAlignThreads)
 
 __global__ void align_scatter_kernel(const int* __restrict__ ids, int numel, int E,
                                      const int* __restrict__ rank, const int* __restrict__ hist,
-                                     int* __restrict__ sorted_ids, int sorted_cap) {
+                                     int* __restrict__ sorted_ids, int sorted_cap,
+                                     int* __restrict__ pos_of) {
   const int i = blockIdx.x * kAlignThreads + threadIdx.x;
   if (i >= numel) return;
   const int e = ids[i];
@@ -184,20 +187,20 @@ __global__ void align_scatter_kernel(const int* __restrict__ ids, int numel, int
   if (e < 0 || e >= E || r < 0) return;
   const int p = hist[(long)blockIdx.x * E + e] + r;
   if (p < sorted_cap) sorted_ids[p] = i;
+  if (pos_of) pos_of[i] = p;
 }
 
 // ---- permutation ------------------------------------------------------------------
 __global__ void permute_rows_kernel(const __nv_bfloat16* __restrict__ src, long ld_src,
                                     const int* __restrict__ sorted_ids, const int* __restrict__ ntp,
                                     int div, int num_valid, __nv_bfloat16* __restrict__ dst,
-                                    long ld_dst, int max_rows, int H, int* __restrict__ pos_of) {
+                                    long ld_dst, int max_rows, int H) {
   const int rows = min(__ldg(ntp), max_rows);
   const int warps = gridDim.x * (blockDim.x >> 5);
   const int nv = H >> 3;
   for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < rows; p += warps) {
     const int id = __ldg(sorted_ids + p);
     if (id >= num_valid) continue;  // dispatch pad: never multiplied, left as is
-    if (pos_of && (threadIdx.x & 31) == 0) pos_of[id] = p;
     uint4* d = reinterpret_cast<uint4*>(dst + (long)p * ld_dst);
     const uint4* s = reinterpret_cast<const uint4*>(src + (long)(id / div) * ld_src);
     for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = __ldg(s + v);
@@ -218,9 +221,10 @@ extern "C" size_t fus_moe_align_workspace(int numel, int E) {
   return sizeof(int) * ((size_t)numel + nchunks * (size_t)E) + 256;
 }
 
-extern "C" int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids,
-                             int sorted_cap, int* expert_ids, int blocks_cap, int* ntp,
-                             void* workspace, size_t ws_bytes, void* stream, int* status) {
+extern "C" int fus_moe_align_pos(const int* ids, int numel, int E, int block_m, int* sorted_ids,
+                                 int sorted_cap, int* expert_ids, int blocks_cap, int* ntp,
+                                 int* pos_of, void* workspace, size_t ws_bytes, void* stream,
+                                 int* status) {
   if (!ids || !sorted_ids || !expert_ids || !ntp || numel < 0 || block_m < 1)
     return set_error(FUS_E_INVALID, "moe_align: bad args");
   if (E < 1 || E > kAlignMaxE) return set_error(FUS_E_UNSUPPORTED, "moe_align: E=%d > %d", E, kAlignMaxE);
@@ -236,7 +240,7 @@ extern "C" int fus_moe_align(const int* ids, int numel, int E, int block_m, int*
       attr_done = true;
     }
     align_small_kernel<<<1, kAlignThreads, sm, st>>>(ids, numel, E, block_m, sorted_ids, sorted_cap,
-                                                    expert_ids, blocks_cap, ntp, status);
+                                                    expert_ids, blocks_cap, ntp, pos_of, status);
     return check_launch("moe_align_small");
   }
   const size_t need = fus_moe_align_workspace(numel, E);
@@ -257,13 +261,20 @@ extern "C" int fus_moe_align(const int* ids, int numel, int E, int block_m, int*
   align_scan_kernel<<<1, kAlignThreads, 0, st>>>(hist, nchunks, E, block_m, numel, sorted_ids,
                                                  sorted_cap, expert_ids, blocks_cap, ntp, status);
   align_scatter_kernel<<<nchunks, kAlignThreads, 0, st>>>(ids, numel, E, rank, hist, sorted_ids,
-                                                          sorted_cap);
+                                                          sorted_cap, pos_of);
   return check_launch("moe_align");
 }
 
-extern "C" int fus_permute_rows_pos(const void* src, long ld_src, const int* sorted_ids,
-                                    const int* ntp, int div, int num_valid, void* dst, long ld_dst,
-                                    int max_rows, int H, int* pos_of, void* stream, int* status) {
+extern "C" int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids,
+                             int sorted_cap, int* expert_ids, int blocks_cap, int* ntp,
+                             void* workspace, size_t ws_bytes, void* stream, int* status) {
+  return fus_moe_align_pos(ids, numel, E, block_m, sorted_ids, sorted_cap, expert_ids, blocks_cap,
+                           ntp, nullptr, workspace, ws_bytes, stream, status);
+}
+
+extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
+                                int div, int num_valid, void* dst, long ld_dst, int max_rows, int H,
+                                void* stream, int* status) {
   (void)status;
   if (!src || !sorted_ids || !ntp || !dst || div < 1 || H <= 0 || H % 8 || max_rows < 0 ||
       !aligned16(src) || !aligned16(dst) || ld_src % 8 || ld_dst % 8)
@@ -274,15 +285,8 @@ extern "C" int fus_permute_rows_pos(const void* src, long ld_src, const int* sor
   if (grid > cap) grid = cap;
   permute_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(
       (const __nv_bfloat16*)src, ld_src, sorted_ids, ntp, div, num_valid, (__nv_bfloat16*)dst,
-      ld_dst, max_rows, H, pos_of);
+      ld_dst, max_rows, H);
   return check_launch("permute_rows");
-}
-
-extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
-                                int div, int num_valid, void* dst, long ld_dst, int max_rows, int H,
-                                void* stream, int* status) {
-  return fus_permute_rows_pos(src, ld_src, sorted_ids, ntp, div, num_valid, dst, ld_dst, max_rows,
-                              H, nullptr, stream, status);
 }
 
 // ---- variant that allocates nothing ---------------------------------------------------

@@ -5,15 +5,17 @@
 //   1 add_rmsnorm            h, r            -> h1, x2
 //   2 router GEMM (tcgen05)  x2, W_g planes  -> fp32 partial logits
 //   3 top-k                  partials, bias  -> topw, topi
-//   4 moe_align              topi            -> sorted ids, expert ids, padded total
+//   4 moe_align              topi            -> sorted ids, expert ids, padded total,
+//                                               pos_of (each pair's dispatch position)
 //      (T <= 16: steps 1-4 are ONE launch, fus_moe_route_small)
 //   5 permute (T > 16)       x2, sorted ids  -> xs (rows in dispatch order)
 //   6 w13 GEMM + SwiGLU      routed rows (T <= 16: gathered from x2 by dispatch position
 //                            with TMA gather4; else xs) and the shared expert's x2 -> act
-//   7 w2 GEMM                routed (act) and shared groups in ONE launch -> y, y_shared
-//   8 merge                  out = bf16(sum_k w_k y_k + h1 + y_shared)
+//   7 w2 GEMM                routed (act) and shared groups in ONE launch -> y (rows in
+//                            dispatch order), y_shared
+//   8 merge                  out = bf16(sum_k w_k y[pos_of[t,k]] + h1 + y_shared)
 //      (T <= 16: fused into step 7 -- the CTA that lands a token tile's last
-//       contribution writes the output for it)
+//       contribution writes the output for it; y is then in pair order)
 //
 // Rounding: only at the tensors the block must store in bf16 (x2, act, y) and at the
 // output. Gate/up feed SwiGLU in fp32, the shared output stays fp32 and the routed sum
@@ -74,8 +76,8 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   L.off_act = take((size_t)L.cap * I * 2);
   L.off_acts = take((size_t)T * I * 2);
   // decode: y[pair] in pair order (fused merge); prefill: the down projection's rows in
-  // dispatch order, in the permuted-row buffer (dead once w13 has read it), gathered back
-  // per token through pos_of by the merge
+  // dispatch order (dense tile stores) in the permuted-row buffer, dead once w13 has
+  // read it; the merge gathers them back per token through pos_of
   L.off_y = small ? take((size_t)L.R * H * 2) : L.off_xs;
   L.off_pos = small ? 0 : take((size_t)L.R * 4);
   L.off_ys = take((size_t)T * H * 4);  // shared expert output, fp32
@@ -134,7 +136,6 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   int* eids = reinterpret_cast<int*>(at(L.off_eids));
   int* ntp = reinterpret_cast<int*>(at(L.off_ntp));
   void* align_ws = at(L.off_align);
-  void* xs = at(L.off_xs);
   void* act = at(L.off_act);
   void* act_s = at(L.off_acts);
   void* y = at(L.off_y);
@@ -142,6 +143,7 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   int* counters = reinterpret_cast<int*>(at(L.off_cnt));
   int* done = reinterpret_cast<int*>(at(L.off_done));
   int* pos_of = reinterpret_cast<int*>(at(L.off_pos));
+  void* xs = at(L.off_xs);
   const bool shared = d->w13s != nullptr;
 
   int rc;
@@ -164,18 +166,18 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
     if ((rc = fus_router_topk(partial, L.nsplit, d->bias, nullptr, topw, topi, T, E, K,
                               d->routed_scale, d->renorm, stream, status)))
       return rc;
-    if ((rc = fus_moe_align(topi, L.R, E, block_n, sorted, L.cap, eids, L.blocks_cap, ntp,
-                            align_ws, fus_moe_align_workspace(L.R, E), stream, status)))
+    if ((rc = fus_moe_align_pos(topi, L.R, E, block_n, sorted, L.cap, eids, L.blocks_cap, ntp,
+                                pos_of, align_ws, fus_moe_align_workspace(L.R, E), stream,
+                                status)))
       return rc;
-    if ((rc = fus_permute_rows_pos(x2, H, sorted, ntp, K, L.R, xs, H, L.cap, H, pos_of, stream,
-                                   status)))
+    if ((rc = fus_permute_rows(x2, H, sorted, ntp, K, L.R, xs, H, L.cap, H, stream, status)))
       return rc;
   }
 
   // weights stream past L2 when a typical expert fills at most one token block
   const int wstream = (double)L.R / E <= block_n ? FUS_GEMM_W_STREAM : 0;
   fus_gemm_group g[2] = {};
-  // ---- w13 + SwiGLU: routed experts over xs, shared expert over x2 ----
+  // ---- w13 + SwiGLU: routed experts over xs (prefill) or x2, shared expert over x2 ----
   g[0].w = d->w13;
   g[0].n_experts = E;
   if (small) {
@@ -186,8 +188,9 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
     g[0].gather_ids = sorted;
     g[0].gather_div = K;
   } else {
-    // prefill: one permutation pass, then dense box loads (gather4 issues one TMA
-    // operation per 4 rows, too many per stage at 128-256 rows)
+    // prefill: one permutation pass, then dense box loads (gather4 moves 4 rows per TMA
+    // operation: 64 operations per stage at 256 rows overwhelm the copy engine, 2.5x
+    // slower than the permuted copy measured at T=2048-8192)
     g[0].x = xs;
     g[0].x_rows = L.cap;
   }

@@ -741,8 +741,7 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
   const int sms = num_sms();
   if (mt2 && epilogue != FUS_EPI_F32 && !merge && pdl == 0 && a.ksplit == 1 &&
       total > 2L * sms &&
-      !(groups[0].flags & FUS_GEMM_NO_PERSIST) && !groups[0].gather_ids &&
-      (ngroups < 2 || !groups[1].gather_ids)) {
+      !(groups[0].flags & FUS_GEMM_NO_PERSIST)) {
     const int grid = (int)(total < sms ? total : sms);
     for (int g = 0; g < ngroups; ++g) {
       const fus_gemm_group& G = groups[g];

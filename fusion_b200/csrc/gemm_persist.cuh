@@ -149,39 +149,70 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const GroupDev& G = args.g[un.gi];
       const int pos0 = un.blk * BN;
       const int n_live = live_columns(G, pos0, BN, lane);
-      if (lane == 0) {
-        const CUtensorMap* tma_a = un.gi ? &ta1 : &ta0;
-        constexpr int kMid = BN < 128 ? BN : 128;  // the tbm maps' box rows
-        const int bx = n_live <= 32 ? 32 : (n_live <= kMid ? kMid : BN);
-        const CUtensorMap* tma_b = bx == 32    ? (un.gi ? &tbs1 : &tbs0)
-                                   : bx == kMid ? (un.gi ? &tbm1 : &tbm0)
-                                                : (un.gi ? &tb1 : &tb0);
-        const uint32_t stage_bytes = Cfg::A_BYTES + (uint32_t)bx * kBK * 2;
-        const uint64_t pol_w = (G.flags & FUS_GEMM_W_STREAM) ? policy_evict_first()
-                                                             : policy_evict_normal();
-        const int ebase = un.expert * args.w_rows;
-        int a_row0, a_row1;
-        if (EPI == FUS_EPI_SWIGLU) {
-          a_row0 = ebase + un.mt * 128;
-          a_row1 = ebase + (args.w_rows >> 1) + un.mt * 128;
-        } else {
-          a_row0 = ebase + un.mt * 256;
-          a_row1 = a_row0 + 128;
+      const CUtensorMap* tma_a = un.gi ? &ta1 : &ta0;
+      constexpr int kMid = BN < 128 ? BN : 128;  // the tbm maps' box rows
+      const int bx = n_live <= 32 ? 32 : (n_live <= kMid ? kMid : BN);
+      const bool gather = G.gather_ids != nullptr;
+      const CUtensorMap* tma_b = gather || bx == BN ? (un.gi ? &tb1 : &tb0)
+                                 : bx == 32         ? (un.gi ? &tbs1 : &tbs0)
+                                                    : (un.gi ? &tbm1 : &tbm0);
+      const uint32_t stage_bytes = Cfg::A_BYTES + (uint32_t)bx * kBK * 2;
+      const uint64_t pol_w = (G.flags & FUS_GEMM_W_STREAM) ? policy_evict_first()
+                                                           : policy_evict_normal();
+      const int ebase = un.expert * args.w_rows;
+      int a_row0, a_row1;
+      if (EPI == FUS_EPI_SWIGLU) {
+        a_row0 = ebase + un.mt * 128;
+        a_row1 = ebase + (args.w_rows >> 1) + un.mt * 128;
+      } else {
+        a_row0 = ebase + un.mt * 256;
+        a_row1 = a_row0 + 128;
+      }
+      // gathered token rows (rows of x picked by dispatch position, one TMA gather4 per
+      // 4 rows, issued by all lanes): lane l owns 4-row groups l and l + 32 of the box
+      int grow[2][4];
+#pragma unroll
+      for (int gq = 0; gq < 2; ++gq)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int j = (lane + 32 * gq) * 4 + q;
+          int row = G.x_rows;  // past the end: zero fill
+          if (gather && j < bx) {
+            const int id = __ldg(G.gather_ids + pos0 + j);
+            if (id < G.live_limit) row = id / G.gather_div;
+          }
+          grow[gq][q] = row;
         }
-        for (int i = 0; i < nk; ++i, ++c) {
-          const int s = c % STAGES;
-          const uint32_t r = c / STAGES;
+      for (int i = 0; i < nk; ++i, ++c) {
+        const int s = c % STAGES;
+        const uint32_t r = c / STAGES;
+        const uint32_t full = bar_full + 8 * s;
+        const int kk = i * kBK;
+        if (lane == 0) {
           if (!mbar_wait_bounded(bar_empty + 8 * s, (r & 1u) ^ 1u, abort_flag, args.status)) {
             stop = true;
-            break;
+          } else {
+            mbar_arrive_expect_tx(full, stage_bytes);
+            const uint32_t a_dst = sA + s * Cfg::A_BYTES;
+            tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
+            tma_load_2d(a_dst + kATileBytes, tma_a, full, kk, a_row1, pol_w);
+            if (!gather) tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, pos0, pol_x);
           }
-          const uint32_t full = bar_full + 8 * s;
-          const int kk = i * kBK;
-          mbar_arrive_expect_tx(full, stage_bytes);
-          const uint32_t a_dst = sA + s * Cfg::A_BYTES;
-          tma_load_2d(a_dst, tma_a, full, kk, a_row0, pol_w);
-          tma_load_2d(a_dst + kATileBytes, tma_a, full, kk, a_row1, pol_w);
-          tma_load_2d(sB + s * Cfg::B_BYTES, tma_b, full, kk % args.K, pos0, pol_x);
+        }
+        if (gather) {
+          // the slot is free (lane 0 waited) and its byte count is posted before any
+          // gathered row can land
+          stop = __shfl_sync(0xffffffffu, (int)stop, 0);
+          if (stop) break;
+#pragma unroll
+          for (int gq = 0; gq < 2; ++gq) {
+            const int grp4 = lane + 32 * gq;
+            if (grp4 * 4 < bx)
+              tma_gather4(sB + s * Cfg::B_BYTES + grp4 * 4 * 128, tma_b, full, kk % args.K,
+                          grow[gq][0], grow[gq][1], grow[gq][2], grow[gq][3], pol_x);
+          }
+        } else if (stop) {
+          break;
         }
       }
       stop = __shfl_sync(0xffffffffu, (int)stop, 0);

@@ -112,15 +112,22 @@ def moe_align_workspace(numel: int, E: int) -> int:
     return int(L.lib().fus_moe_align_workspace(numel, E))
 
 
-def moe_align(ids, E: int, block_m: int, sorted_ids, expert_ids, ntp, workspace=None):
+def moe_align(ids, E: int, block_m: int, sorted_ids, expert_ids, ntp, workspace=None,
+              pos_of=None):
+    """Dispatch layout; with ``pos_of`` also each pair's dispatch position."""
     flat = ids.reshape(-1)
     assert flat.is_contiguous() and flat.dtype == torch.int32
     need = moe_align_workspace(flat.numel(), E)
     if need and (workspace is None or workspace.numel() < need):
         workspace = torch.empty(need, dtype=torch.uint8, device=ids.device)
-    L.call("fus_moe_align", _p(flat), flat.numel(), E, block_m, _p(sorted_ids), sorted_ids.numel(),
-           _p(expert_ids), expert_ids.numel(), _p(ntp), _p(workspace) if need else None,
-           need, _stream(), _sp())
+    if pos_of is None:
+        L.call("fus_moe_align", _p(flat), flat.numel(), E, block_m, _p(sorted_ids),
+               sorted_ids.numel(), _p(expert_ids), expert_ids.numel(), _p(ntp),
+               _p(workspace) if need else None, need, _stream(), _sp())
+    else:
+        L.call("fus_moe_align_pos", _p(flat), flat.numel(), E, block_m, _p(sorted_ids),
+               sorted_ids.numel(), _p(expert_ids), expert_ids.numel(), _p(ntp), _p(pos_of),
+               _p(workspace) if need else None, need, _stream(), _sp())
 
 
 def route_small(h, r, gamma, wa, nplanes: int, bias, h1, x2, logits, topw, topi, block_m: int,
@@ -142,16 +149,6 @@ def permute_rows(src, sorted_ids, ntp, div: int, num_valid: int, dst, max_rows: 
         max_rows = min(dst.shape[0], sorted_ids.numel())
     L.call("fus_permute_rows", _p(src), _ld(src), _p(sorted_ids), _p(ntp), div, num_valid, _p(dst),
            _ld(dst), max_rows, H, _stream(), _sp())
-
-
-def permute_rows_pos(src, sorted_ids, ntp, div: int, num_valid: int, dst, pos_of,
-                     max_rows: int | None = None):
-    """permute_rows that also records pos_of[sorted_ids[p]] = p for the live positions."""
-    H = src.shape[1]
-    if max_rows is None:
-        max_rows = min(dst.shape[0], sorted_ids.numel())
-    L.call("fus_permute_rows_pos", _p(src), _ld(src), _p(sorted_ids), _p(ntp), div, num_valid,
-           _p(dst), _ld(dst), max_rows, H, _p(pos_of), _stream(), _sp())
 
 
 def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map=None,

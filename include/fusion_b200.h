@@ -119,6 +119,11 @@ size_t fus_moe_align_workspace(int numel, int E);
 int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids, int sorted_cap,
                   int* expert_ids, int blocks_cap, int* ntp, void* workspace, size_t ws_bytes,
                   void* stream, int* status);
+/* Same, and records each pair's dispatch position: pos_of[i] = p where sorted_ids[p] = i
+ * (pos_of has numel entries; holes and invalid ids are left untouched). */
+int fus_moe_align_pos(const int* ids, int numel, int E, int block_m, int* sorted_ids,
+                      int sorted_cap, int* expert_ids, int blocks_cap, int* ntp, int* pos_of,
+                      void* workspace, size_t ws_bytes, void* stream, int* status);
 
 /* Same result as fus_moe_align, but the call allocates nothing and takes no workspace.
  * No counterpart in the reference. It is for callers that cannot allocate device
@@ -153,17 +158,11 @@ int fus_moe_route_small(const void* h, const void* r, const void* gamma, float e
 /* Row permutation into dispatch order (the A gather `offs_token // top_k` of
  * glm52/kernels/moe_gateup.py:96-99, done once up front so the GEMM reads dense rows):
  *   dst[p] = src[sorted_ids[p] / div]  if sorted_ids[p] < num_valid,
- * for p < min(ntp[0], max_rows); pad rows are left untouched (the GEMMs neither
- * multiply nor write dispatch pads). H % 8 == 0, 16-byte aligned rows. */
+ * for p < min(ntp[0], max_rows); pad rows are left untouched (the GEMMs do not
+ * multiply dispatch pads). H % 8 == 0, 16-byte aligned rows. */
 int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp, int div,
                      int num_valid, void* dst, long ld_dst, int max_rows, int H, void* stream,
                      int* status);
-/* Same, and records where each pair landed: pos_of[sorted_ids[p]] = p for the live
- * positions p (pos_of has num_valid entries). With the down projection's rows stored in
- * dispatch order, fus_merge_pos gathers them back per token through pos_of. */
-int fus_permute_rows_pos(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
-                         int div, int num_valid, void* dst, long ld_dst, int max_rows, int H,
-                         int* pos_of, void* stream, int* status);
 
 /* ---------------------------------------------------------------------------------
  * Grouped expert GEMM on tcgen05 tensor cores (replaces the Triton grouped GEMMs
@@ -272,7 +271,7 @@ int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long l
               const void* res, long ldr, const void* extra, long lde, int extra_f32, void* out,
               long ldo, int T, int H, int round_mid, void* stream, int* status);
 /* fus_merge over expert rows stored in dispatch order: row (t, k) is
- * y + pos_of[t*K + k]*ldy (round_mid = 0). */
+ * y + pos_of[t*K + k]*ldy (round_mid = 0); pos_of as written by fus_moe_align_pos. */
 int fus_merge_pos(const void* y, long ldy, const int* pos_of, int K, const float* w, long ldw,
                   const void* res, long ldr, const void* extra, long lde, int extra_f32,
                   void* out, long ldo, int T, int H, void* stream, int* status);

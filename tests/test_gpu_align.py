@@ -82,3 +82,23 @@ def test_permute_rows():
         else:
             pass  # dispatch pad: left untouched
     assert torch.all(dst[rs.size:].cpu() == 7.0)  # rows past ntp untouched
+
+
+@pytest.mark.parametrize("T,bm", [(50, 16), (8192, 256)])  # one-CTA and multi-launch paths
+def test_align_pos_of_inverts_sorted_ids(T, bm):
+    """pos_of[i] is the dispatch position of pair i: sorted_ids[pos_of[i]] == i, and
+    the layout itself is the oracle's bit for bit."""
+    K, E = 8, 256
+    rng = np.random.default_rng(5 + T)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    rs, re, rn = O.moe_align_block_size(ids, bm, E)
+    t = torch.from_numpy(ids).to(DEV)
+    s = torch.empty(rs.size, dtype=torch.int32, device=DEV)
+    e = torch.empty(re.size, dtype=torch.int32, device=DEV)
+    ntp = torch.zeros(1, dtype=torch.int32, device=DEV)
+    pos = torch.full((T * K,), -1, dtype=torch.int32, device=DEV)
+    ops.moe_align(t, E, bm, s, e, ntp, pos_of=pos)
+    finish()
+    assert np.array_equal(s.cpu().numpy(), rs) and np.array_equal(e.cpu().numpy(), re)
+    p = pos.cpu().numpy()
+    assert np.array_equal(rs[p], np.arange(T * K))

@@ -147,15 +147,18 @@ def test_gathered_rows_equal_permuted_rows(bn):
 
 
 @pytest.mark.parametrize("bn", [64, 128, 256])
-@pytest.mark.parametrize("epi", ["swiglu", "bf16"])
+@pytest.mark.parametrize("epi", ["swiglu", "swiglu_gather", "bf16", "bf16_dense"])
 def test_persistent_equals_one_tile_per_cta(bn, epi):
     """The persistent prefill kernel (one CTA per SM looping over tiles) gives the same
-    bits as one tile per CTA, routed + dense groups, with row map / scale / fp32 output."""
+    bits as one tile per CTA, routed + dense groups: permuted or gathered token rows,
+    scattered rows with row map / scale, dense rows in dispatch order (TMA tile stores),
+    fp32 output."""
     T, K, E, H, I = 512, 8, 16, 2048, 1024
     ids, s, eids, ntp, cap = layout(T, K, E, bn, 3 + bn)
     R = T * K
     maxb = min(R, E) + R // bn
-    if epi == "swiglu":
+    if epi.startswith("swiglu"):
+        gather = epi == "swiglu_gather"
         x = (torch.randn(T, H, device=DEV)).to(torch.bfloat16)
         w = (torch.randn(E, 2 * I, H, device=DEV) * 0.03).to(torch.bfloat16)
         ws = (torch.randn(2 * I, H, device=DEV) * 0.03).to(torch.bfloat16)
@@ -165,9 +168,10 @@ def test_persistent_equals_one_tile_per_cta(bn, epi):
         for flag in (0, ops.GEMM_NO_PERSIST):
             a = torch.zeros(cap, I, dtype=torch.bfloat16, device=DEV)
             a_s = torch.zeros(T, I, dtype=torch.bfloat16, device=DEV)
-            gs = [ops.gemm_group(w, xs, a, expert_ids=eids, ntp=ntp, max_blocks=maxb,
-                                 row_limit=cap, live_ids=s, live_limit=R,
-                                 flags=flag | ops.GEMM_SWIGLU_EXACT),
+            gs = [ops.gemm_group(w, x if gather else xs, a, expert_ids=eids, ntp=ntp,
+                                 max_blocks=maxb, row_limit=cap, live_ids=s, live_limit=R,
+                                 flags=flag | ops.GEMM_SWIGLU_EXACT,
+                                 gather_ids=s if gather else None, gather_div=K),
                   ops.gemm_group(ws, x, a_s, max_blocks=-(-T // bn), row_limit=T,
                                  flags=ops.GEMM_SWIGLU_EXACT)]
             ops.grouped_gemm(gs, 2 * I, H, ops.FUS_EPI_SWIGLU, bn)
@@ -183,22 +187,33 @@ def test_persistent_equals_one_tile_per_cta(bn, epi):
         ws = (torch.randn(H, I, device=DEV) * 0.03).to(torch.bfloat16)
         scale = torch.rand(R, device=DEV)
         outs = []
+        dense = epi == "bf16_dense"
         for flag in (0, ops.GEMM_NO_PERSIST):
-            y = torch.zeros(R, H, dtype=torch.bfloat16, device=DEV)
+            y = torch.zeros(cap if dense else R, H, dtype=torch.bfloat16, device=DEV)
             ys = torch.zeros(T, H, dtype=torch.float32, device=DEV)
-            gs = [ops.gemm_group(w, a, y, expert_ids=eids, ntp=ntp, max_blocks=maxb, row_map=s,
-                                 row_limit=R, row_scale=scale, live_ids=s, live_limit=R,
-                                 flags=flag),
+            if dense:  # rows stay in dispatch order
+                g0 = ops.gemm_group(w, a, y, expert_ids=eids, ntp=ntp, max_blocks=maxb,
+                                    row_limit=cap, live_ids=s, live_limit=R, flags=flag)
+            else:
+                g0 = ops.gemm_group(w, a, y, expert_ids=eids, ntp=ntp, max_blocks=maxb,
+                                    row_map=s, row_limit=R, row_scale=scale, live_ids=s,
+                                    live_limit=R, flags=flag)
+            gs = [g0,
                   ops.gemm_group(ws, a_s, ys, max_blocks=-(-T // bn), row_limit=T,
                                  flags=ops.GEMM_OUT_F32)]
             ops.grouped_gemm(gs, H, I, ops.FUS_EPI_BF16, bn)
             outs.append((y, ys))
         finish()
-        assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
         assert torch.equal(outs[0][1], outs[1][1])
         ref = ref_rows(a, w, eids.cpu(), bn, lambda aa, ww: aa @ ww.t())
         sc = s.cpu().numpy()
         valid = torch.from_numpy(np.nonzero(sc < R)[0]).to(DEV)
-        yref = torch.zeros(R, H, device=DEV)
-        yref[s[valid].long()] = ref[valid] * scale[s[valid].long()][:, None]
-        assert rel_err(outs[0][0].float().cpu().numpy(), yref.cpu().numpy()) < 1e-2
+        if dense:  # pad rows of the dense output are unspecified: compare live rows
+            y0, y1 = outs[0][0][valid], outs[1][0][valid]
+            assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+            assert rel_err(y0.float().cpu().numpy(), ref[valid].cpu().numpy()) < 1e-2
+        else:
+            assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
+            yref = torch.zeros(R, H, device=DEV)
+            yref[s[valid].long()] = ref[valid] * scale[s[valid].long()][:, None]
+            assert rel_err(outs[0][0].float().cpu().numpy(), yref.cpu().numpy()) < 1e-2

@@ -120,3 +120,26 @@ def test_add_and_seed():
     assert np.array_equal(to_np(o), O.bf16(to_np(a) + to_np(b)))
     assert torch.count_nonzero(s) == 0
     assert torch.equal(s2, a)
+
+
+@pytest.mark.parametrize("T", [3, 600])
+def test_merge_pos_equals_merge_over_pair_order(T):
+    """Merging rows stored in dispatch order through pos_of gives the bits of merging
+    the same rows in pair order (same summation order)."""
+    K, H = 8, 6144
+    g = torch.Generator(device="cpu").manual_seed(T)
+    R = T * K
+    rows = R + 37  # dispatch order with room for pads
+    perm = torch.randperm(rows, generator=g)[:R].to(torch.int32)  # pos_of
+    y_disp = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    y_pair = y_disp[perm.long()]
+    w = torch.rand(T, K, generator=g)
+    h1 = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    ys = torch.randn(T, H, generator=g)
+    y_disp, y_pair, perm, w, h1, ys = (a.to(DEV) for a in (y_disp, y_pair, perm, w, h1, ys))
+    o1 = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    o2 = torch.empty_like(o1)
+    ops.merge(y_pair.view(T, K, H), w, h1, ys, o1, round_mid=False)
+    ops.merge_pos(y_disp, perm, K, w, h1, ys, o2)
+    finish()
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))

@@ -97,7 +97,7 @@ SIGNATURES: dict[str, tuple] = {
     "fus_router_topk": (i32, [vp, i32, vp, vp, vp, vp, i32, i32, i32, f32, i32, vp, vp]),
     "fus_moe_align_workspace": (sz, [i32, i32]),
     "fus_moe_align": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, sz, vp, vp]),
-    "fus_moe_align_pos": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp, sz, vp, vp]),
+    "fus_moe_align_ex": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, i32, vp, sz, vp, vp]),
     "fus_moe_align_noalloc": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp]),
     "fus_moe_route_small": (i32, [vp, vp, vp, f32, vp, i32, vp, i32, i32, i32, i32, f32, i32, vp, vp,
                                   vp, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, i32, vp, vp]),

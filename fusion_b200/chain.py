@@ -121,7 +121,8 @@ class BlockChain:
                 ("router_topk", lambda: ops.router_topk(self.partial, self.nsplit, bias, None,
                                                         o.topw, o.topi)),
                 ("moe_align", lambda: ops.moe_align(o.topi, E, bn, self.sorted, self.eids,
-                                                    self.ntp, self.align_ws, self.pos_of)),
+                                                    self.ntp, self.align_ws, self.pos_of,
+                                                    ops.ALIGN_BALANCED)),
                 ("permute", lambda: ops.permute_rows(self.x2, self.sorted, self.ntp, K, self.R,
                                                      self.xs, self.cap)),
             ]

@@ -67,11 +67,23 @@ __device__ void rank_chunk(const int* __restrict__ ids, int base, int numel, int
   __syncthreads();  // wcnt is cleared by the next chunk
 }
 
+// Position of an expert's q-th pair (stable order) inside its padded region. Reference
+// layout: start + q, pads after the last pair. Balanced layout (FUS_ALIGN_BALANCED):
+// the c pairs are spread evenly over the region's nb = ceil(c / block_m) blocks,
+// pb = ceil(c / nb) per block with the block's pads after them, so no block holds only
+// a few stragglers (each block streams the expert's full weights through the GEMM).
+__device__ __forceinline__ int place_pair(int start, int q, int c, int block_m, int balanced) {
+  if (!balanced) return start + q;
+  const int nb = (c + block_m - 1) / block_m;
+  const int pb = (c + nb - 1) / nb;
+  return start + (q / pb) * block_m + (q % pb);
+}
+
 // Per-expert padded placement from counts (cnt[e]); writes start[e], ntp, expert_ids
 // and the pad sentinels. Needs E <= blockDim.x * 1 handled by a strided loop + scan.
 __device__ void place_experts(const int* cnt, int* start, int E, int block_m, int numel,
                               int* sorted_ids, int sorted_cap, int* expert_ids, int blocks_cap,
-                              int* ntp, int* scan_tmp, int* status) {
+                              int* ntp, int* scan_tmp, int* status, int balanced) {
   const int tid = threadIdx.x;
   // exclusive scan of padded counts (E <= 1024: one element per thread)
   int padded = 0;
@@ -95,8 +107,19 @@ __device__ void place_experts(const int* cnt, int* start, int E, int block_m, in
     const int s = incl - padded;
     for (int b = s / block_m; b < (s + padded) / block_m; ++b)
       if (b < blocks_cap) expert_ids[b] = tid;
-    for (int p = s + cnt[tid]; p < s + padded; ++p)
-      if (p < sorted_cap) sorted_ids[p] = numel;
+    const int c = cnt[tid];
+    if (!balanced) {
+      for (int p = s + c; p < s + padded; ++p)
+        if (p < sorted_cap) sorted_ids[p] = numel;
+    } else {
+      const int nb = padded / block_m;
+      const int pb = (c + nb - 1) / nb;
+      for (int b = 0; b < nb; ++b) {
+        const int live = max(0, min(pb, c - b * pb));
+        for (int p = s + b * block_m + live; p < s + (b + 1) * block_m; ++p)
+          if (p < sorted_cap) sorted_ids[p] = numel;
+      }
+    }
   }
   __syncthreads();
 }
@@ -105,7 +128,7 @@ __global__ void __launch_bounds__(kAlignThreads)
     align_small_kernel(const int* __restrict__ ids, int numel, int E, int block_m,
                        int* __restrict__ sorted_ids, int sorted_cap, int* __restrict__ expert_ids,
                        int blocks_cap, int* __restrict__ ntp, int* __restrict__ pos_of,
-                       int* status) {
+                       int balanced, int* status) {
   extern __shared__ int sm[];
   int* wcnt = sm;                            // [32][E]
   int* cursor = wcnt + kAlignWarps * E;      // [E]
@@ -125,11 +148,11 @@ __global__ void __launch_bounds__(kAlignThreads)
   }
   __syncthreads();
   place_experts(cursor, start, E, block_m, numel, sorted_ids, sorted_cap, expert_ids, blocks_cap,
-                ntp, scan_tmp, status);
+                ntp, scan_tmp, status, balanced);
   for (int i = threadIdx.x; i < numel; i += kAlignThreads) {
     const int e = eid[i];
     if (e < 0) continue;
-    const int p = start[e] + rank[i];
+    const int p = place_pair(start[e], rank[i], cursor[e], block_m, balanced);
     if (p < sorted_cap) sorted_ids[p] = i;
     if (pos_of) pos_of[i] = p;
   }
@@ -156,7 +179,8 @@ __global__ void __launch_bounds__(kAlignThreads)
 __global__ void __launch_bounds__(kAlignThreads)
     align_scan_kernel(int* __restrict__ hist, int nchunks, int E, int block_m, int numel,
                       int* __restrict__ sorted_ids, int sorted_cap, int* __restrict__ expert_ids,
-                      int blocks_cap, int* __restrict__ ntp, int* status) {
+                      int blocks_cap, int* __restrict__ ntp, int* __restrict__ se, int balanced,
+                      int* status) {
   __shared__ int cnt[kAlignMaxE];
   __shared__ int start[kAlignMaxE];
   __shared__ int scan_tmp[kAlignThreads];
@@ -171,21 +195,26 @@ __global__ void __launch_bounds__(kAlignThreads)
   }
   __syncthreads();
   place_experts(cnt, start, E, block_m, numel, sorted_ids, sorted_cap, expert_ids, blocks_cap, ntp,
-                scan_tmp, status);
-  for (int x = threadIdx.x; x < E; x += kAlignThreads)
-    for (int c = 0; c < nchunks; ++c) hist[(long)c * E + x] += start[x];
+                scan_tmp, status, balanced);
+  // hist[c][e] stays the expert-relative rank of chunk c's first pair; se = (start, count)
+  for (int x = threadIdx.x; x < E; x += kAlignThreads) {
+    se[2 * x] = start[x];
+    se[2 * x + 1] = cnt[x];
+  }
 }
 
 __global__ void align_scatter_kernel(const int* __restrict__ ids, int numel, int E,
                                      const int* __restrict__ rank, const int* __restrict__ hist,
                                      int* __restrict__ sorted_ids, int sorted_cap,
-                                     int* __restrict__ pos_of) {
+                                     int* __restrict__ pos_of, const int* __restrict__ se,
+                                     int block_m, int balanced) {
   const int i = blockIdx.x * kAlignThreads + threadIdx.x;
   if (i >= numel) return;
   const int e = ids[i];
   const int r = rank[i];
   if (e < 0 || e >= E || r < 0) return;
-  const int p = hist[(long)blockIdx.x * E + e] + r;
+  const int p = place_pair(__ldg(se + 2 * e), hist[(long)blockIdx.x * E + e] + r,
+                          __ldg(se + 2 * e + 1), block_m, balanced);
   if (p < sorted_cap) sorted_ids[p] = i;
   if (pos_of) pos_of[i] = p;
 }
@@ -218,15 +247,17 @@ using namespace fus;
 extern "C" size_t fus_moe_align_workspace(int numel, int E) {
   if (numel <= kAlignSmallMax) return 0;
   const size_t nchunks = (size_t)ceil_div(numel, kAlignThreads);
-  return sizeof(int) * ((size_t)numel + nchunks * (size_t)E) + 256;
+  return sizeof(int) * ((size_t)numel + nchunks * (size_t)E + 2 * (size_t)E) + 256;
 }
 
-extern "C" int fus_moe_align_pos(const int* ids, int numel, int E, int block_m, int* sorted_ids,
-                                 int sorted_cap, int* expert_ids, int blocks_cap, int* ntp,
-                                 int* pos_of, void* workspace, size_t ws_bytes, void* stream,
-                                 int* status) {
-  if (!ids || !sorted_ids || !expert_ids || !ntp || numel < 0 || block_m < 1)
+extern "C" int fus_moe_align_ex(const int* ids, int numel, int E, int block_m, int* sorted_ids,
+                                int sorted_cap, int* expert_ids, int blocks_cap, int* ntp,
+                                int* pos_of, int flags, void* workspace, size_t ws_bytes,
+                                void* stream, int* status) {
+  if (!ids || !sorted_ids || !expert_ids || !ntp || numel < 0 || block_m < 1 ||
+      (flags & ~FUS_ALIGN_BALANCED))
     return set_error(FUS_E_INVALID, "moe_align: bad args");
+  const int balanced = (flags & FUS_ALIGN_BALANCED) ? 1 : 0;
   if (E < 1 || E > kAlignMaxE) return set_error(FUS_E_UNSUPPORTED, "moe_align: E=%d > %d", E, kAlignMaxE);
   cudaStream_t st = as_stream(stream);
   if (numel <= kAlignSmallMax) {
@@ -240,7 +271,8 @@ extern "C" int fus_moe_align_pos(const int* ids, int numel, int E, int block_m, 
       attr_done = true;
     }
     align_small_kernel<<<1, kAlignThreads, sm, st>>>(ids, numel, E, block_m, sorted_ids, sorted_cap,
-                                                    expert_ids, blocks_cap, ntp, pos_of, status);
+                                                    expert_ids, blocks_cap, ntp, pos_of, balanced,
+                                                    status);
     return check_launch("moe_align_small");
   }
   const size_t need = fus_moe_align_workspace(numel, E);
@@ -249,6 +281,7 @@ extern "C" int fus_moe_align_pos(const int* ids, int numel, int E, int block_m, 
   const int nchunks = ceil_div(numel, kAlignThreads);
   int* rank = reinterpret_cast<int*>(workspace);
   int* hist = rank + numel;
+  int* se = hist + (size_t)nchunks * E;
   const size_t sm = sizeof(int) * ((size_t)kAlignWarps * E + E);
   static bool attr_done2 = false;
   if (!attr_done2) {
@@ -259,17 +292,19 @@ extern "C" int fus_moe_align_pos(const int* ids, int numel, int E, int block_m, 
   }
   align_rank_kernel<<<nchunks, kAlignThreads, sm, st>>>(ids, numel, E, rank, hist, status);
   align_scan_kernel<<<1, kAlignThreads, 0, st>>>(hist, nchunks, E, block_m, numel, sorted_ids,
-                                                 sorted_cap, expert_ids, blocks_cap, ntp, status);
+                                                 sorted_cap, expert_ids, blocks_cap, ntp, se,
+                                                 balanced, status);
   align_scatter_kernel<<<nchunks, kAlignThreads, 0, st>>>(ids, numel, E, rank, hist, sorted_ids,
-                                                          sorted_cap, pos_of);
+                                                          sorted_cap, pos_of, se, block_m,
+                                                          balanced);
   return check_launch("moe_align");
 }
 
 extern "C" int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids,
                              int sorted_cap, int* expert_ids, int blocks_cap, int* ntp,
                              void* workspace, size_t ws_bytes, void* stream, int* status) {
-  return fus_moe_align_pos(ids, numel, E, block_m, sorted_ids, sorted_cap, expert_ids, blocks_cap,
-                           ntp, nullptr, workspace, ws_bytes, stream, status);
+  return fus_moe_align_ex(ids, numel, E, block_m, sorted_ids, sorted_cap, expert_ids, blocks_cap,
+                          ntp, nullptr, 0, workspace, ws_bytes, stream, status);
 }
 
 extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_ids, const int* ntp,
@@ -292,13 +327,14 @@ extern "C" int fus_permute_rows(const void* src, long ld_src, const int* sorted_
 // ---- variant that allocates nothing ---------------------------------------------------
 // Scratch for the multi-launch path (stable ranks + per-chunk histograms) lives in a
 // file-scope device array sized for the largest input this variant accepts: numel up to
-// 65536 (T = 8192 tokens at top-8) and up to 512 experts, 393,472 bytes. Every GPU that
+// 65536 (T = 8192 tokens at top-8) and up to 512 experts, 397,568 bytes. Every GPU that
 // loads the library holds it until the process exits.
 namespace fus {
 constexpr int kAlignNoAllocMaxNumel = 65536;
 constexpr size_t kAlignNoAllocBytes =
     sizeof(int) * ((size_t)kAlignNoAllocMaxNumel +
-                   (size_t)(kAlignNoAllocMaxNumel / kAlignThreads) * kAlignMaxE) + 256;
+                   (size_t)(kAlignNoAllocMaxNumel / kAlignThreads) * kAlignMaxE + 2 * kAlignMaxE) +
+    256;
 static __device__ __align__(256) unsigned char g_align_scratch[kAlignNoAllocBytes];
 
 // Host code cannot use g_align_scratch as a device address (on the host the name is only

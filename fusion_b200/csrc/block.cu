@@ -166,9 +166,11 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
     if ((rc = fus_router_topk(partial, L.nsplit, d->bias, nullptr, topw, topi, T, E, K,
                               d->routed_scale, d->renorm, stream, status)))
       return rc;
-    if ((rc = fus_moe_align_pos(topi, L.R, E, block_n, sorted, L.cap, eids, L.blocks_cap, ntp,
-                                pos_of, align_ws, fus_moe_align_workspace(L.R, E), stream,
-                                status)))
+    // balanced layout: an expert just over a block fills two even blocks, not a full
+    // block plus a few stragglers that stream the same weights again
+    if ((rc = fus_moe_align_ex(topi, L.R, E, block_n, sorted, L.cap, eids, L.blocks_cap, ntp,
+                               pos_of, FUS_ALIGN_BALANCED, align_ws,
+                               fus_moe_align_workspace(L.R, E), stream, status)))
       return rc;
     if ((rc = fus_permute_rows(x2, H, sorted, ntp, K, L.R, xs, H, L.cap, H, stream, status)))
       return rc;

@@ -112,22 +112,26 @@ def moe_align_workspace(numel: int, E: int) -> int:
     return int(L.lib().fus_moe_align_workspace(numel, E))
 
 
+ALIGN_BALANCED = 0x1
+
+
 def moe_align(ids, E: int, block_m: int, sorted_ids, expert_ids, ntp, workspace=None,
-              pos_of=None):
-    """Dispatch layout; with ``pos_of`` also each pair's dispatch position."""
+              pos_of=None, flags: int = 0):
+    """Dispatch layout; with ``pos_of`` also each pair's dispatch position, with
+    ``flags=ALIGN_BALANCED`` each expert's pairs spread evenly over its blocks."""
     flat = ids.reshape(-1)
     assert flat.is_contiguous() and flat.dtype == torch.int32
     need = moe_align_workspace(flat.numel(), E)
     if need and (workspace is None or workspace.numel() < need):
         workspace = torch.empty(need, dtype=torch.uint8, device=ids.device)
-    if pos_of is None:
+    if pos_of is None and not flags:
         L.call("fus_moe_align", _p(flat), flat.numel(), E, block_m, _p(sorted_ids),
                sorted_ids.numel(), _p(expert_ids), expert_ids.numel(), _p(ntp),
                _p(workspace) if need else None, need, _stream(), _sp())
     else:
-        L.call("fus_moe_align_pos", _p(flat), flat.numel(), E, block_m, _p(sorted_ids),
+        L.call("fus_moe_align_ex", _p(flat), flat.numel(), E, block_m, _p(sorted_ids),
                sorted_ids.numel(), _p(expert_ids), expert_ids.numel(), _p(ntp), _p(pos_of),
-               _p(workspace) if need else None, need, _stream(), _sp())
+               flags, _p(workspace) if need else None, need, _stream(), _sp())
 
 
 def route_small(h, r, gamma, wa, nplanes: int, bias, h1, x2, logits, topw, topi, block_m: int,

@@ -119,18 +119,23 @@ size_t fus_moe_align_workspace(int numel, int E);
 int fus_moe_align(const int* ids, int numel, int E, int block_m, int* sorted_ids, int sorted_cap,
                   int* expert_ids, int blocks_cap, int* ntp, void* workspace, size_t ws_bytes,
                   void* stream, int* status);
-/* Same, and records each pair's dispatch position: pos_of[i] = p where sorted_ids[p] = i
- * (pos_of has numel entries; holes and invalid ids are left untouched). */
-int fus_moe_align_pos(const int* ids, int numel, int E, int block_m, int* sorted_ids,
-                      int sorted_cap, int* expert_ids, int blocks_cap, int* ntp, int* pos_of,
-                      void* workspace, size_t ws_bytes, void* stream, int* status);
+/* Same, with options. pos_of (optional, numel entries): each pair's dispatch position,
+ * pos_of[i] = p where sorted_ids[p] = i (holes / invalid ids left untouched).
+ * flags: FUS_ALIGN_BALANCED spreads each expert's c pairs evenly over its
+ * nb = ceil(c / block_m) blocks (ceil(c / nb) per block, each block's pads after its
+ * pairs) instead of filling blocks in order; padded sizes, expert_ids and ntp are
+ * unchanged. Not the reference's layout: for callers that own the layout (the block). */
+#define FUS_ALIGN_BALANCED 0x1
+int fus_moe_align_ex(const int* ids, int numel, int E, int block_m, int* sorted_ids,
+                     int sorted_cap, int* expert_ids, int blocks_cap, int* ntp, int* pos_of,
+                     int flags, void* workspace, size_t ws_bytes, void* stream, int* status);
 
 /* Same result as fus_moe_align, but the call allocates nothing and takes no workspace.
  * No counterpart in the reference. It is for callers that cannot allocate device
  * memory: engines whose memory pool owns nearly all of HBM from start-up (the KV cache
  * takes what is left, so a later cudaMalloc fails), and callers that cannot pay the
  * device-wide synchronisation cudaMalloc / cudaFree imply inside a serving loop.
- * Scratch is a fixed array inside the library (393,472 bytes on every GPU that loads
+ * Scratch is a fixed array inside the library (397,568 bytes on every GPU that loads
  * it, held until the process exits), so the limits are numel <= 65536 (T <= 8192 at
  * top-8) and E <= 512; larger inputs are rejected with FUS_E_UNSUPPORTED. The first
  * call on each device looks up the array's device address (cudaGetSymbolAddress) with
@@ -271,7 +276,7 @@ int fus_merge(const void* y, long ld_t, long ld_k, int K, const float* w, long l
               const void* res, long ldr, const void* extra, long lde, int extra_f32, void* out,
               long ldo, int T, int H, int round_mid, void* stream, int* status);
 /* fus_merge over expert rows stored in dispatch order: row (t, k) is
- * y + pos_of[t*K + k]*ldy (round_mid = 0); pos_of as written by fus_moe_align_pos. */
+ * y + pos_of[t*K + k]*ldy (round_mid = 0); pos_of as written by fus_moe_align_ex. */
 int fus_merge_pos(const void* y, long ldy, const int* pos_of, int K, const float* w, long ldw,
                   const void* res, long ldr, const void* extra, long lde, int extra_f32,
                   void* out, long ldo, int T, int H, void* stream, int* status);

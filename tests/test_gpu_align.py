@@ -102,3 +102,52 @@ def test_align_pos_of_inverts_sorted_ids(T, bm):
     assert np.array_equal(s.cpu().numpy(), rs) and np.array_equal(e.cpu().numpy(), re)
     p = pos.cpu().numpy()
     assert np.array_equal(rs[p], np.arange(T * K))
+
+
+def balanced_layout_np(ids: np.ndarray, bm: int, E: int):
+    """CPU statement of FUS_ALIGN_BALANCED: the reference's padded regions, each
+    expert's c pairs spread over its nb = ceil(c/bm) blocks, ceil(c/nb) per block."""
+    s_ref, e_ref, n_ref = O.moe_align_block_size(ids, bm, E)
+    flat = ids.reshape(-1)
+    numel = flat.size
+    out = np.full_like(s_ref, numel)
+    order = np.argsort(flat, kind="stable")
+    counts = np.bincount(flat, minlength=E)
+    start, src = 0, 0
+    for e in range(E):
+        c = int(counts[e])
+        padded = -(-c // bm) * bm
+        if c:
+            nb = padded // bm
+            pb = -(-c // nb)
+            for q in range(c):
+                out[start + (q // pb) * bm + q % pb] = order[src + q]
+        start += padded
+        src += c
+    return out, e_ref, n_ref
+
+
+@pytest.mark.parametrize("T,bm,skew", [(60, 64, False), (8192, 256, False), (8192, 256, True),
+                                       (3000, 128, True)])
+def test_align_balanced_layout(T, bm, skew):
+    """FUS_ALIGN_BALANCED: same padded regions / expert ids / ntp as the reference
+    layout, pairs spread evenly over each expert's blocks, pos_of its inverse."""
+    K, E = 8, 256
+    rng = np.random.default_rng(17 + T + bm)
+    if skew:  # a few hot experts with several blocks each
+        p = 1.0 / np.arange(1, E + 1) ** 1.1
+        ids = np.stack([rng.choice(E, K, replace=False, p=p / p.sum()) for _ in range(T)])
+    else:
+        ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)])
+    ids = ids.astype(np.int32)
+    rs, re, rn = balanced_layout_np(ids, bm, E)
+    t = torch.from_numpy(ids).to(DEV)
+    s = torch.empty(rs.size, dtype=torch.int32, device=DEV)
+    e = torch.empty(re.size, dtype=torch.int32, device=DEV)
+    ntp = torch.zeros(1, dtype=torch.int32, device=DEV)
+    pos = torch.full((T * K,), -1, dtype=torch.int32, device=DEV)
+    ops.moe_align(t, E, bm, s, e, ntp, pos_of=pos, flags=ops.ALIGN_BALANCED)
+    finish()
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(e.cpu().numpy(), re) and int(ntp.item()) == int(rn[0])
+    assert np.array_equal(rs[pos.cpu().numpy()], np.arange(T * K))

@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--regimes", default=",".join(REGIMES),
                     help="extra T values measured besides the headline ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1 decode row exchange: NVLink peer stores or NCCL all_to_all")
     return ap.parse_args()
 
 
@@ -204,7 +206,8 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
     import torch.distributed as dist
 
     from fusion_b200 import ops, synth, traffic
-    from fusion_b200.ep import CudaEPBackend, EPDecodeGraph, ExpertParallelMoE, shard_weights
+    from fusion_b200.ep import (CudaEPBackend, EPDecodeGraph, EPDecodeStep, ExpertParallelMoE,
+                                shard_weights)
 
     dims = synth.Dims()
     w = shard_weights(SEED, rank, world, dims, "cuda")
@@ -214,13 +217,20 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     pk = traffic.peaks()
 
+    def decode_step(T: int):
+        # p2p: the whole step as one library call (PDL-chained, NVLink exchange);
+        # nccl: the Python-composed step with all_to_all; both replayed from a CUDA graph
+        if args.ep_exchange == "p2p":
+            return EPDecodeStep(be, T).capture()
+        return EPDecodeGraph(ep, T, dims.H, "cuda", exchange="nccl")
+
     def measure(T: int, steps: int, warmup: int) -> dict:
         if rank == 0:
             print(f"[bench ep{world}] T={T}/rank", file=sys.stderr, flush=True)
         h, r = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cuda")
         small = T <= 16
         if small:  # fixed-slot exchange recorded in a CUDA graph (no host sync)
-            g = EPDecodeGraph(ep, T, dims.H, "cuda")
+            g = decode_step(T)
             g.h.copy_(h)
             g.r.copy_(r)
             run = g.replay
@@ -241,7 +251,11 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
             b.record()
             b.synchronize()
             ms.append(a.elapsed_time(b))
-        res = g.res if small else ep(h, r)
+        res = ({"topi": g.topi} if isinstance(g, EPDecodeStep) else g.res) if small else ep(h, r)
+        torch.cuda.synchronize()
+        ops.check_status()
+        if small and g.x is not None:
+            g.x.close()
         barrier()
         ms_step = max_over_ranks(statistics.fmean(ms))
         # distinct experts over the whole job: union of every rank's routed ids
@@ -275,7 +289,7 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
     rd = torch.empty_like(hd)
     evs = []
     barrier()
-    ge = EPDecodeGraph(ep, T, dims.H, "cuda")
+    ge = decode_step(T)
     for _ in range(args.steps):
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -286,9 +300,15 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
         b.record()
         b.synchronize()
         evs.append(a.elapsed_time(b))
+    torch.cuda.synchronize()
+    ops.check_status()
+    if ge.x is not None:
+        ge.x.close()
     barrier()
     e2e_ms = max_over_ranks(statistics.fmean(evs))
     if rank == 0:
+        exch = ("NVLink peer stores into CUDA-IPC exchange buffers, bounded flag waits"
+                if args.ep_exchange == "p2p" else "NCCL all_to_all")
         line = {
             "metric": METRIC, "value": head["tokens_per_s"], "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3),
@@ -301,8 +321,9 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
                        "topk": dims.topk, "experts_per_gpu": dims.E // world,
                        "l2": "flushed by a 512 MB write before every timed step",
                        "parallelism": f"ep{world}",
-                       "timing": "T<=16: fixed-slot EP step (NCCL all_to_all) replayed from a "
-                                 "CUDA graph; larger T: eager EP step; CUDA events"},
+                       "timing": f"T<=16: fixed-slot EP step ({exch}) replayed from a "
+                                 "CUDA graph; larger T: eager EP step (NCCL all_to_all); "
+                                 "CUDA events"},
             "us_per_block": head["us_per_block"],
             "roofline": {"kernel": "whole EP block step (per GPU)", "bound": "hbm",
                          "achieved": head["algorithmic_GB_per_gpu"] / (head["ms_per_step"] / 1e3),
@@ -313,8 +334,10 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
             "cpu_baseline": None,
             "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": hh.numel() * 4, "d2h_bytes_per_step": out_h.numel() * 2,
-                    "api": "fusion_b200.ep.EPDecodeGraph (ExpertParallelMoE.forward_fixed)"},
-            "gpu_launches": 11 * args.steps,
+                    "api": ("fusion_b200.ep.EPDecodeStep -> fus_ep_p2p_decode_forward (C ABI)"
+                            if args.ep_exchange == "p2p" else
+                            "fusion_b200.ep.EPDecodeGraph (ExpertParallelMoE.forward_fixed)")},
+            "gpu_launches": (7 if args.ep_exchange == "p2p" else 11) * args.steps,
             "clocks": clk.summary(),
             "regimes": regimes,
         }

@@ -84,6 +84,29 @@ class BlockDesc(C.Structure):
     ]
 
 
+class EPP2PDesc(C.Structure):
+    """Mirror of ``fus_ep_p2p_desc``."""
+
+    _fields_ = [
+        ("blk", C.POINTER(BlockDesc)),
+        ("E_loc", i32),
+        ("W", i32),
+        ("rank", i32),
+        ("S", i32),
+        ("peer_rows", vp),
+        ("peer_leid", vp),
+        ("peer_dflags", vp),
+        ("peer_ret", vp),
+        ("peer_cflags", vp),
+        ("recv_rows", vp),
+        ("recv_leid", vp),
+        ("ret_rows", vp),
+        ("dflags", vp),
+        ("cflags", vp),
+        ("epoch", vp),
+    ]
+
+
 # name -> (restype, argtypes). Every symbol of include/fusion_b200.h appears here.
 SIGNATURES: dict[str, tuple] = {
     "fus_version": (i32, []),
@@ -126,6 +149,15 @@ SIGNATURES: dict[str, tuple] = {
                                     vp]),
     "fus_ep_pack": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, i64, vp, vp, vp]),
     "fus_ep_unpack": (i32, [vp, i64, i32, vp, i32, vp, i64, vp, vp]),
+    "fus_ipc_handle": (i32, [vp, vp, C.POINTER(C.c_size_t)]),
+    "fus_ipc_open": (i32, [vp, sz, C.POINTER(C.c_void_p)]),
+    "fus_ipc_close": (i32, [vp, sz]),
+    "fus_ep_p2p_dispatch": (i32, [vp, i64, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp,
+                                  vp, vp, vp]),
+    "fus_ep_p2p_wait": (i32, [vp, vp, i32, u64, vp, vp]),
+    "fus_ep_p2p_combine": (i32, [vp, i64, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp]),
+    "fus_ep_p2p_decode_workspace": (sz, [vp, i32]),
+    "fus_ep_p2p_decode_forward": (i32, [vp, vp, vp, i32, vp, vp, vp, vp, vp, sz, vp, vp]),
     "fus_synth_fill": (i32, [vp, i32, i64, i64, u64, f32, f32, vp]),
     "fus_synth_fill_host": (None, [vp, i32, i64, i64, u64, f32, f32]),
 }

@@ -124,11 +124,11 @@ __device__ void place_experts(const int* cnt, int* start, int E, int block_m, in
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kAlignThreads)
-    align_small_kernel(const int* __restrict__ ids, int numel, int E, int block_m,
-                       int* __restrict__ sorted_ids, int sorted_cap, int* __restrict__ expert_ids,
-                       int blocks_cap, int* __restrict__ ntp, int* __restrict__ pos_of,
-                       int balanced, int* status) {
+__device__ void align_small_body(const int* __restrict__ ids, int numel, int E, int block_m,
+                                 int* __restrict__ sorted_ids, int sorted_cap,
+                                 int* __restrict__ expert_ids, int blocks_cap,
+                                 int* __restrict__ ntp, int* __restrict__ pos_of, int balanced,
+                                 int* status) {
   extern __shared__ int sm[];
   int* wcnt = sm;                            // [32][E]
   int* cursor = wcnt + kAlignWarps * E;      // [E]
@@ -156,6 +156,42 @@ __global__ void __launch_bounds__(kAlignThreads)
     if (p < sorted_cap) sorted_ids[p] = i;
     if (pos_of) pos_of[i] = p;
   }
+}
+
+__global__ void __launch_bounds__(kAlignThreads)
+    align_small_kernel(const int* __restrict__ ids, int numel, int E, int block_m,
+                       int* __restrict__ sorted_ids, int sorted_cap, int* __restrict__ expert_ids,
+                       int blocks_cap, int* __restrict__ ntp, int* __restrict__ pos_of,
+                       int balanced, int* status) {
+  align_small_body(ids, numel, E, block_m, sorted_ids, sorted_cap, expert_ids, blocks_cap, ntp,
+                   pos_of, balanced, status);
+}
+
+// The same after `flags[w] >= *epoch` for every w < W (the expert-parallel receive
+// side: ids are the received local expert ids, written by the peers before they raise
+// their flag). A wait that runs out sets FUS_ERR_TIMEOUT and the layout is built from
+// what arrived.
+__global__ void __launch_bounds__(kAlignThreads)
+    align_small_after_flags_kernel(const int* flags, const int* epoch, int W,
+                                   const int* __restrict__ ids, int numel, int E, int block_m,
+                                   int* __restrict__ sorted_ids, int sorted_cap,
+                                   int* __restrict__ expert_ids, int blocks_cap,
+                                   int* __restrict__ ntp, int* status) {
+  pdl_wait();  // the epoch is bumped by the predecessor (the dispatch)
+  if ((int)threadIdx.x < W) {
+    const int e = *epoch;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys_i32(flags + threadIdx.x) < e) {
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        raise_status(status, FUS_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  align_small_body(ids, numel, E, block_m, sorted_ids, sorted_cap, expert_ids, blocks_cap, ntp,
+                   nullptr, 0, status);
+  pdl_allow_dependents();
 }
 
 // ---- large inputs: 3 launches ------------------------------------------------------
@@ -243,6 +279,40 @@ size_t small_smem_bytes(int E) {
 }  // namespace fus
 
 using namespace fus;
+
+namespace fus {
+int moe_align_small_after_flags(const int* flags, const int* epoch, int W, const int* ids,
+                                int numel, int E, int block_m, int* sorted_ids, int sorted_cap,
+                                int* expert_ids, int blocks_cap, int* ntp, int pdl, void* stream,
+                                int* status) {
+  if (numel > kAlignSmallMax || E < 1 || E > kAlignMaxE || W > kAlignThreads)
+    return set_error(FUS_E_UNSUPPORTED, "moe_align_after_flags: numel=%d E=%d W=%d", numel, E, W);
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(align_small_after_flags_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)small_smem_bytes(kAlignMaxE));
+  });
+  if (attr_err != cudaSuccess)
+    return set_error(FUS_E_LAUNCH, "moe_align attr: %s", cudaGetErrorString(attr_err));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kAlignThreads);
+  cfg.dynamicSmemBytes = small_smem_bytes(E);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, align_small_after_flags_kernel, flags, epoch, W, ids,
+                                     numel, E, block_m, sorted_ids, sorted_cap, expert_ids,
+                                     blocks_cap, ntp, status);
+  if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "moe_align_after_flags: %s", cudaGetErrorString(e));
+  return check_launch("moe_align_after_flags");
+}
+}  // namespace fus
 
 extern "C" size_t fus_moe_align_workspace(int numel, int E) {
   if (numel <= kAlignSmallMax) return 0;

@@ -42,6 +42,16 @@ constexpr uint64_t kWaitBudgetNs = 1000000000ull;
 // predecessor grid completed and its writes are visible, `pdl_allow_dependents` lets
 // the next kernel start launching. Both are no-ops without the launch attribute.
 // ------------------------------------------------------------------------------------
+// system-scope acquire / release on a flag another GPU writes / reads
+FUS_DEVICE int ld_acquire_sys_i32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+FUS_DEVICE void st_release_sys_i32(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 FUS_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 FUS_DEVICE void pdl_allow_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

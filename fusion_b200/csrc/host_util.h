@@ -33,6 +33,18 @@ int grouped_gemm_launch(const fus_gemm_group* groups, int ngroups, int w_rows, i
                         int group_blocks, const fus_merge_spec* merge, int pdl, void* stream,
                         int* status);
 
+// expert-parallel receive side: the single-CTA dispatch layout of `ids` after every
+// flags[w] >= *epoch (w < W), and the merge over rows in dispatch order after the same
+// kind of wait (pdl: launched as a programmatic dependent of the previous kernel)
+int moe_align_small_after_flags(const int* flags, const int* epoch, int W, const int* ids,
+                                int numel, int E, int block_m, int* sorted_ids, int sorted_cap,
+                                int* expert_ids, int blocks_cap, int* ntp, int pdl, void* stream,
+                                int* status);
+int merge_pos_after_flags(const void* y, long ldy, const int* pos_of, int K, const float* w,
+                          long ldw, const void* res, long ldr, const void* extra, long lde,
+                          int extra_f32, void* out, long ldo, int T, int H, const int* flags,
+                          const int* epoch, int W, int pdl, void* stream, int* status);
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }

@@ -95,7 +95,24 @@ __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, lon
                              const int* __restrict__ pos_of, const float* __restrict__ w, long ldw,
                              const __nv_bfloat16* __restrict__ res, long ldr,
                              const void* __restrict__ extra, long lde, int extra_f32,
-                             __nv_bfloat16* __restrict__ out, long ldo, int H, int round_mid) {
+                             __nv_bfloat16* __restrict__ out, long ldo, int H, int round_mid,
+                             const int* flags, const int* epoch, int W, int* status) {
+  // expert-parallel combine: wait until every owner raised flags[w] >= *epoch (their
+  // rows are in y); bounded, FUS_ERR_TIMEOUT when it runs out
+  if (flags) {
+    pdl_wait();
+    if ((int)threadIdx.x < W) {
+      const int e = *epoch;
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys_i32(flags + threadIdx.x) < e) {
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+          raise_status(status, FUS_ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+    __syncthreads();
+  }
   const int t = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c >= H) return;
@@ -233,7 +250,8 @@ extern "C" int fus_silu_and_mul(const void* x, long ldx, void* y, long ldy, int 
 static int merge_launch(const void* y, long ld_t, long ld_k, int K, const int* pos_of,
                         const float* w, long ldw, const void* res, long ldr, const void* extra,
                         long lde, int extra_f32, void* out, long ldo, int T, int H, int round_mid,
-                        void* stream) {
+                        void* stream, const int* flags = nullptr, const int* epoch = nullptr,
+                        int W = 0, int pdl = 0, int* status = nullptr) {
   if (T < 0 || H <= 0 || H % 8 || K < 0) return set_error(FUS_E_INVALID, "merge: bad shape");
   if (K > 0 && (!y || !aligned16(y) || ld_t % 8 || ld_k % 8))
     return set_error(FUS_E_INVALID, "merge: y rows must be 16-byte aligned");
@@ -243,14 +261,20 @@ static int merge_launch(const void* y, long ld_t, long ld_k, int K, const int* p
   if (T == 0) return FUS_OK;
   cudaStream_t st = as_stream(stream);
   dim3 grid = row_grid(T, H, 128);
-  if (K == 8)
-    merge_kernel<8><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, pos_of, w, ldw, (const bf16*)res,
-                                          ldr, extra, lde, extra_f32, (bf16*)out, ldo, H,
-                                          round_mid);
-  else
-    merge_kernel<0><<<grid, 128, 0, st>>>((const bf16*)y, ld_t, ld_k, K, pos_of, w, ldw, (const bf16*)res,
-                                          ldr, extra, lde, extra_f32, (bf16*)out, ldo, H,
-                                          round_mid);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, K == 8 ? merge_kernel<8> : merge_kernel<0>,
+                                       (const bf16*)y, ld_t, ld_k, K, pos_of, w, ldw,
+                                       (const bf16*)res, ldr, extra, lde, extra_f32, (bf16*)out,
+                                       ldo, H, round_mid, flags, epoch, W, status);
+  if (err != cudaSuccess) return set_error(FUS_E_LAUNCH, "merge: %s", cudaGetErrorString(err));
   return check_launch("merge");
 }
 
@@ -262,6 +286,18 @@ extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float
   return merge_launch(y, ld_t, ld_k, K, nullptr, w, ldw, res, ldr, extra, lde, extra_f32, out, ldo,
                       T, H, round_mid, stream);
 }
+
+namespace fus {
+int merge_pos_after_flags(const void* y, long ldy, const int* pos_of, int K, const float* w,
+                          long ldw, const void* res, long ldr, const void* extra, long lde,
+                          int extra_f32, void* out, long ldo, int T, int H, const int* flags,
+                          const int* epoch, int W, int pdl, void* stream, int* status) {
+  if (!flags || !epoch || W < 1 || W > 128)
+    return set_error(FUS_E_INVALID, "merge_after_flags: bad flags");
+  return merge_launch(y, 0, ldy, K, pos_of, w, ldw, res, ldr, extra, lde, extra_f32, out, ldo, T,
+                      H, 0, stream, flags, epoch, W, pdl, status);
+}
+}  // namespace fus
 
 extern "C" int fus_merge_pos(const void* y, long ldy, const int* pos_of, int K, const float* w,
                              long ldw, const void* res, long ldr, const void* extra, long lde,

@@ -48,23 +48,10 @@ struct RouteArgs {
   int* status;
 };
 
-__device__ float block_sum_256(float v, float* red) {
-  v = warp_sum(v);
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) red[w] = v;
-  __syncthreads();
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kRouteThreads / 32; ++i) s += red[i];
-  __syncthreads();
-  return s;
-}
-
 __global__ void __launch_bounds__(kRouteThreads)
     route_small_kernel(const __grid_constant__ RouteArgs a) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(dsm);  // [T][H]: h1, then x2
-  __shared__ float red[kRouteThreads / 32];
   __shared__ float rstd_s[kRouteMaxT];
   __shared__ float part[kRouteThreads / 32][kRouteExperts * kRouteMaxT];
   __shared__ int is_last;
@@ -78,6 +65,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   // in flight at once) while the CTA normalises
   constexpr int kMaxChunks = 4;  // H <= 4 * 8 * 256 = 8192
   uint4 wq[kMaxChunks][3];
+  uint4 gq[kMaxChunks];  // the norm weight, for step 2
 #pragma unroll
   for (int ci = 0; ci < kMaxChunks; ++ci) {
     const int c = tid + ci * kRouteThreads;
@@ -86,35 +74,60 @@ __global__ void __launch_bounds__(kRouteThreads)
       if (c < nv && p < a.nplanes)
         wq[ci][p] = __ldg(reinterpret_cast<const uint4*>(a.wa + (long)e0 * a.nplanes * H +
                                                          (long)p * H + c * 8));
+    if (c < nv) gq[ci] = __ldg(reinterpret_cast<const uint4*>(a.gamma) + c);
+  }
+  // the correction bias of experts lane*8 .. lane*8+7, for the selection (whichever CTA
+  // turns out to be the last one needs it; loading it now takes it off the tail)
+  float bq[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = lane * 8 + j;
+    bq[j] = (a.bias && e < E) ? __ldg(a.bias + e) : 0.f;
   }
 
   // ---- 1. h1 = bf16(h + r) into shared memory, sum of squares per token ----
+  // per-warp partial sums per token (no block barrier between tokens); one reduction
+  // across the warps for all T afterwards
   for (int t = 0; t < T; ++t) {
     float ss = 0.f;
-    for (int c = tid; c < nv; c += kRouteThreads) {
-      float x[8], rr[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(a.h + (long)t * H) + c), x);
-      unpack8(__ldg(reinterpret_cast<const uint4*>(a.r + (long)t * H) + c), rr);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        x[e] = round_bf(x[e] + rr[e]);
-        ss += x[e] * x[e];
+    for (int ci = 0; ci < kMaxChunks; ++ci) {
+      const int c = tid + ci * kRouteThreads;
+      if (c < nv) {
+        float x[8], rr[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(a.h + (long)t * H) + c), x);
+        unpack8(__ldg(reinterpret_cast<const uint4*>(a.r + (long)t * H) + c), rr);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          x[e] = round_bf(x[e] + rr[e]);
+          ss += x[e] * x[e];
+        }
+        const uint4 v = pack8(x);
+        reinterpret_cast<uint4*>(xs + (long)t * H)[c] = v;
+        if (writer) reinterpret_cast<uint4*>(a.h1 + (long)t * H)[c] = v;
       }
-      const uint4 v = pack8(x);
-      reinterpret_cast<uint4*>(xs + (long)t * H)[c] = v;
-      if (writer) reinterpret_cast<uint4*>(a.h1 + (long)t * H)[c] = v;
     }
-    ss = block_sum_256(ss, red);
-    if (tid == 0) rstd_s[t] = 1.0f / sqrtf(ss / (float)H + a.eps);
+    ss = warp_sum(ss);
+    if (lane == 0) part[warp][t] = ss;
+  }
+  __syncthreads();
+  if (tid < T) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRouteThreads / 32; ++w) v += part[w][tid];
+    rstd_s[tid] = 1.0f / sqrtf(v / (float)H + a.eps);
   }
   __syncthreads();
   // ---- 2. x2 = bf16(bf16(h1 * rstd) * gamma), in place ----
   for (int t = 0; t < T; ++t) {
     const float rs = rstd_s[t];
-    for (int c = tid; c < nv; c += kRouteThreads) {
+#pragma unroll
+    for (int ci = 0; ci < kMaxChunks; ++ci) {
+      const int c = tid + ci * kRouteThreads;
+      if (c >= nv) break;
       float x[8], g[8];
       unpack8(reinterpret_cast<const uint4*>(xs + (long)t * H)[c], x);
-      unpack8(__ldg(reinterpret_cast<const uint4*>(a.gamma) + c), g);
+      unpack8(gq[ci], g);
 #pragma unroll
       for (int e = 0; e < 8; ++e) x[e] = round_bf(x[e] * rs) * g[e];
       const uint4 v = pack8(x);
@@ -129,16 +142,20 @@ __global__ void __launch_bounds__(kRouteThreads)
   for (int e = 0; e < kRouteExperts; ++e)
 #pragma unroll
     for (int t = 0; t < kRouteMaxT; ++t) acc[e][t] = 0.f;
+#pragma unroll
   for (int ci = 0; ci < kMaxChunks; ++ci) {
     const int c = tid + ci * kRouteThreads;
     if (c >= nv) break;
     float w[kRouteExperts][8];
     unpack8(wq[ci][0], w[0]);
-    for (int p = 1; p < a.nplanes; ++p) {
-      float q[8];
-      unpack8(wq[ci][p], q);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[0][i] += q[i];
+    for (int p = 1; p < 3; ++p) {
+      if (p < a.nplanes) {
+        float q[8];
+        unpack8(wq[ci][p], q);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[0][i] += q[i];
+      }
     }
 #pragma unroll
     for (int t = 0; t < kRouteMaxT; ++t) {
@@ -183,31 +200,46 @@ __global__ void __launch_bounds__(kRouteThreads)
   int* scan = start + 256;                    // [256]
   const int e8 = lane * 8;
   for (int t = warp; t < T; t += kRouteThreads / 32) {
+    // lane l holds experts 8l .. 8l+7: unbiased score sc, selection score ch
     float sc[8], ch[8];
+    int ix[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int e = e8 + j;
+      ix[j] = e;
       if (e < E) {
         const float l = __ldcg(a.logits + (long)t * E + e);
         sc[j] = 1.0f / (1.0f + expf(-l));
-        ch[j] = sc[j] + (a.bias ? __ldg(a.bias + e) : 0.f);
+        ch[j] = sc[j] + bq[j];
       } else {
         sc[j] = 0.f;
         ch[j] = -INFINITY;
+        ix[j] = 0x7fffffff;
       }
     }
-    unsigned used = 0;
+    // sort the lane's 8 descending by (ch, then lower expert id): odd-even transposition
+#pragma unroll
+    for (int pass = 0; pass < 8; ++pass)
+#pragma unroll
+      for (int j = pass & 1; j + 1 < 8; j += 2) {
+        const bool sw = ch[j + 1] > ch[j] || (ch[j + 1] == ch[j] && ix[j + 1] < ix[j]);
+        if (sw) {
+          const float tc = ch[j], ts = sc[j];
+          const int ti = ix[j];
+          ch[j] = ch[j + 1];
+          sc[j] = sc[j + 1];
+          ix[j] = ix[j + 1];
+          ch[j + 1] = tc;
+          sc[j + 1] = ts;
+          ix[j + 1] = ti;
+        }
+      }
+    // topk rounds: the warp's best head wins (ties -> lower expert id), its lane pops it
     float my_w = 0.f, wsum = 0.f;
     int my_id = 0;
     for (int k = 0; k < a.topk; ++k) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (!(used & (1u << j)) && e8 + j < E && (ch[j] > bv || bi == 0x7fffffff)) {
-          bv = ch[j];
-          bi = e8 + j;
-        }
+      float bv = ch[0];
+      int bi = ix[0];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -218,14 +250,17 @@ __global__ void __launch_bounds__(kRouteThreads)
         }
       }
       const int owner = bi >> 3;
-      float s_win = 0.f;
+      const float s_win = __shfl_sync(0xffffffffu, sc[0], owner & 31);
+      if (lane == owner) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (lane == owner && bi == e8 + j) {
-          used |= 1u << j;
-          s_win = sc[j];
+        for (int j = 0; j < 7; ++j) {
+          ch[j] = ch[j + 1];
+          sc[j] = sc[j + 1];
+          ix[j] = ix[j + 1];
         }
-      s_win = __shfl_sync(0xffffffffu, s_win, owner & 31);
+        ch[7] = -INFINITY;
+        ix[7] = 0x7fffffff;
+      }
       wsum += s_win;
       if (lane == k) {
         my_w = s_win;

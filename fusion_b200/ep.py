@@ -16,7 +16,10 @@ block on its own tokens (weak scaling):
 
 The exchange logic is written once (`ExpertParallelMoE`) over a backend that supplies
 the local compute: `CudaEPBackend` (the sm_100a kernels) here; the CPU tests run the same
-exchange over gloo with a numpy backend. The reference has no multi-GPU path
+exchange over gloo with a numpy backend. Small batches (decode) exchange fixed slot
+blocks: over NCCL all_to_all (`forward_fixed`), or with `P2PExchange` by direct stores
+into the peers' exchange buffers over NVLink and flag waits (`forward_p2p`, no
+collective launch at all). The reference has no multi-GPU path
 (log/LOG-00-plan-and-filter.md:41); SURVEY §8e gives the design.
 """
 
@@ -93,24 +96,194 @@ class ExpertParallelMoE:
     __call__ = forward
 
 
-class EPDecodeGraph:
-    """`forward_fixed` for a fixed T recorded in a CUDA graph (NCCL all_to_all included);
-    copy inputs into `h` / `r`, call `replay()`, read `out`."""
+    def forward_p2p(self, h: torch.Tensor, r: torch.Tensor, x: "P2PExchange") -> dict:
+        """`forward_fixed` with the three all_to_alls replaced by peer stores into the
+        exchange buffers and flag waits (x.S >= T*topk slots per source)."""
+        be = self.be
+        h1, x2, topw, topi = be.route(h, r)
+        T, K = topi.shape
+        shared = be.shared_begin(x2)
+        slots = torch.empty(T * K, dtype=torch.int32, device=x2.device)
+        ops.ep_p2p_dispatch(x2, topi, be.E_loc, x.W, x.S, x.rank, x.peer_rows, x.peer_leid,
+                            x.peer_dflags, x.epoch, slots)
+        ops.ep_p2p_wait(x.dflags, x.epoch, x.W)
+        y_recv = be.local_experts_holes(x.recv_rows, x.recv_leid)
+        ops.ep_p2p_combine(y_recv, x.recv_leid, x.W, x.S, x.rank, x.peer_ret, x.peer_cflags,
+                           x.epoch)
+        ops.ep_p2p_wait(x.cflags, x.epoch, x.W)
+        ys = be.shared_end(shared)
+        out = torch.empty_like(h1)
+        ops.merge_pos(x.ret_rows, slots, K, topw, h1, ys, out)
+        return {"out": out, "h1": h1, "topw": topw, "topi": topi}
 
-    def __init__(self, ep: ExpertParallelMoE, T: int, H: int, device):
-        self.ep = ep
-        self.h = torch.zeros(T, H, dtype=torch.bfloat16, device=device)
+
+class P2PExchange:
+    """This rank's exchange buffer, exported through CUDA IPC, and the addresses of every
+    rank's (W ranks of one node, S slots per source, H features). Layout per rank:
+    recv_rows [W*S, H] bf16, recv_leid [W*S] int32, ret_rows [W*S, H] bf16, dflags [W],
+    cflags [W] int32; plus a local step counter (epoch). Collective: every rank of the
+    group constructs it together."""
+
+    def __init__(self, S: int, H: int, device, group=None):
+        self.group = group
+        self.W = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.S, self.H = S, H
+        W, n = self.W, self.W * S
+        offs, o = {}, 0
+        for name, nbytes in (("recv_rows", n * H * 2), ("recv_leid", n * 4),
+                             ("ret_rows", n * H * 2), ("dflags", W * 4), ("cflags", W * 4)):
+            offs[name] = o
+            o = (o + nbytes + 255) // 256 * 256
+        self.buf = torch.zeros(o, dtype=torch.uint8, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        b = self.buf
+        self.recv_rows = b[offs["recv_rows"]:offs["recv_rows"] + n * H * 2].view(torch.bfloat16).view(n, H)
+        self.recv_leid = b[offs["recv_leid"]:offs["recv_leid"] + n * 4].view(torch.int32)
+        self.ret_rows = b[offs["ret_rows"]:offs["ret_rows"] + n * H * 2].view(torch.bfloat16).view(n, H)
+        self.dflags = b[offs["dflags"]:offs["dflags"] + W * 4].view(torch.int32)
+        self.cflags = b[offs["cflags"]:offs["cflags"] + W * 4].view(torch.int32)
+        torch.cuda.synchronize(device)
+        handle, off = ops.ipc_handle(self.buf)
+        if self.W > 1:
+            allh = [None] * self.W
+            dist.all_gather_object(allh, (handle, off), group=group)
+        else:
+            allh = [(handle, off)]
+        self._opened = []
+        bases = []
+        for w, (h, o_) in enumerate(allh):
+            if w == self.rank:
+                bases.append(self.buf.data_ptr())
+            else:
+                p = ops.ipc_open(h, o_)
+                self._opened.append((p, o_))
+                bases.append(p)
+
+        def table(name):
+            return torch.tensor([bb + offs[name] for bb in bases], dtype=torch.int64,
+                                device=device)
+
+        self.peer_rows, self.peer_leid = table("recv_rows"), table("recv_leid")
+        self.peer_ret, self.peer_dflags, self.peer_cflags = (table("ret_rows"), table("dflags"),
+                                                             table("cflags"))
+        if self.W > 1:
+            dist.barrier(group=group)  # every buffer zeroed and mapped before any store
+
+    def close(self):
+        """Unmap the peers' buffers (collective; no step may be in flight)."""
+        torch.cuda.synchronize()
+        if self.W > 1:
+            dist.barrier(group=self.group)
+        for p, o in self._opened:
+            ops.ipc_close(p, o)
+        self._opened = []
+
+
+class EPDecodeStep:
+    """The decode step of one rank as ONE library call (fus_ep_p2p_decode_forward: seven
+    launches chained with programmatic dependent launch over the NVLink exchange) for a
+    fixed T; `capture()` records it in a CUDA graph. Collective: every rank builds it."""
+
+    def __init__(self, be: "CudaEPBackend", T: int, group=None):
+        import ctypes
+
+        from . import _lib as L
+
+        self.be, self.T = be, T
+        self.x = P2PExchange(T * be.topk, be.H, be.dev, group)
+        d = L.BlockDesc()
+        d.H, d.I, d.E, d.topk = be.H, be.I, be.E, be.topk
+        d.eps, d.routed_scale, d.renorm = be.eps, be.scale, 1
+        d.gamma, d.wa, d.nplanes = be.gamma.data_ptr(), be.wa.data_ptr(), be.nplanes
+        d.bias = be.bias.data_ptr() if be.bias is not None else None
+        d.w13, d.w2 = be.w13.data_ptr(), be.w2.data_ptr()
+        d.w13s = be.w13s.data_ptr() if be.w13s is not None else None
+        d.w2s = be.w2s.data_ptr() if be.w2s is not None else None
+        self._blk = d
+        x = self.x
+        p = L.EPP2PDesc()
+        p.blk = ctypes.pointer(d)
+        p.E_loc, p.W, p.rank, p.S = be.E_loc, x.W, x.rank, x.S
+        p.peer_rows, p.peer_leid, p.peer_dflags = (x.peer_rows.data_ptr(), x.peer_leid.data_ptr(),
+                                                   x.peer_dflags.data_ptr())
+        p.peer_ret, p.peer_cflags = x.peer_ret.data_ptr(), x.peer_cflags.data_ptr()
+        p.recv_rows, p.recv_leid, p.ret_rows = (x.recv_rows.data_ptr(), x.recv_leid.data_ptr(),
+                                                x.ret_rows.data_ptr())
+        p.dflags, p.cflags, p.epoch = x.dflags.data_ptr(), x.cflags.data_ptr(), x.epoch.data_ptr()
+        self.desc = p
+        nbytes = int(L.lib().fus_ep_p2p_decode_workspace(ctypes.byref(p), T))
+        if nbytes == 0:
+            raise ValueError("ep_p2p_decode: bad sizes")
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=be.dev)
+        bf = torch.bfloat16
+        self.h = torch.zeros(T, be.H, dtype=bf, device=be.dev)
         self.r = torch.zeros_like(self.h)
+        self.out = torch.empty_like(self.h)
+        self.h1 = torch.empty_like(self.h)
+        self.topw = torch.empty(T, be.topk, dtype=torch.float32, device=be.dev)
+        self.topi = torch.empty(T, be.topk, dtype=torch.int32, device=be.dev)
+        self.graph = None
+
+    def forward(self) -> torch.Tensor:
+        """One step on the inputs in `h` / `r`; returns `out` (also fills h1/topw/topi)."""
+        import ctypes
+
+        from . import _lib as L
+
+        L.call("fus_ep_p2p_decode_forward", ctypes.byref(self.desc), self.h.data_ptr(),
+               self.r.data_ptr(), self.T, self.out.data_ptr(), self.h1.data_ptr(),
+               self.topw.data_ptr(), self.topi.data_ptr(), self.ws.data_ptr(),
+               self.ws.numel(), torch.cuda.current_stream().cuda_stream,
+               ops.status_tensor().data_ptr())
+        return self.out
+
+    def capture(self):
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             for _ in range(2):
-                ep.forward_fixed(self.h, self.r)
+                self.forward()
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.res = ep.forward_fixed(self.h, self.r)
+            self.forward()
+        return self
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
+
+    def close(self):
+        self.x.close()
+
+
+class EPDecodeGraph:
+    """The fixed-slot decode step for a fixed T recorded in a CUDA graph; copy inputs into
+    `h` / `r`, call `replay()`, read `out`. exchange="p2p": NVLink peer stores
+    (`forward_p2p`), "nccl": all_to_all (`forward_fixed`)."""
+
+    def __init__(self, ep: ExpertParallelMoE, T: int, H: int, device, exchange: str = "p2p"):
+        self.ep = ep
+        self.h = torch.zeros(T, H, dtype=torch.bfloat16, device=device)
+        self.r = torch.zeros_like(self.h)
+        self.x = None
+        if exchange == "p2p":
+            self.x = P2PExchange(T * ep.be.topk, H, device, ep.group)
+            step = lambda: ep.forward_p2p(self.h, self.r, self.x)  # noqa: E731
+        else:
+            step = lambda: ep.forward_fixed(self.h, self.r)  # noqa: E731
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.res = step()
         self.out = self.res["out"]
 
     def replay(self):

@@ -281,6 +281,45 @@ def ep_unpack(rows, send_ids, n: int, y):
 
 
 # -------------------------------------------------------------------------------------
+# NVLink peer-memory exchange (CUDA IPC)
+def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """CUDA IPC handle (64 bytes) of the allocation holding ``t`` and t's offset in it."""
+    h = (C.c_char * 64)()
+    off = C.c_size_t(0)
+    L.call("fus_ipc_handle", _p(t), C.cast(h, C.c_void_p), C.byref(off))
+    return bytes(h), int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Map a peer's exported allocation; returns the device address of its offset."""
+    h = (C.c_char * 64).from_buffer_copy(handle)
+    ptr = C.c_void_p(0)
+    L.call("fus_ipc_open", C.cast(h, C.c_void_p), offset, C.byref(ptr))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int, offset: int):
+    L.call("fus_ipc_close", ptr, offset)
+
+
+def ep_p2p_dispatch(x, topi, E_loc: int, W: int, S: int, rank: int, peer_rows, peer_leid,
+                    peer_flags, epoch, slot_of_pair):
+    T, K = topi.shape
+    L.call("fus_ep_p2p_dispatch", _p(x), _ld(x), x.shape[1], _p(topi), T, K, E_loc, W, S, rank,
+           _p(peer_rows), _p(peer_leid), _p(peer_flags), _p(epoch), _p(slot_of_pair),
+           _stream(), _sp())
+
+
+def ep_p2p_wait(flags, epoch, W: int, timeout_ns: int = 0):
+    L.call("fus_ep_p2p_wait", _p(flags), _p(epoch), W, timeout_ns, _stream(), _sp())
+
+
+def ep_p2p_combine(y, recv_leid, W: int, S: int, rank: int, peer_ret, peer_cflags, epoch):
+    L.call("fus_ep_p2p_combine", _p(y), _ld(y), y.shape[1], _p(recv_leid), W, S, rank,
+           _p(peer_ret), _p(peer_cflags), _p(epoch), _stream(), _sp())
+
+
+# -------------------------------------------------------------------------------------
 def synth_fill(t: torch.Tensor, seed: int, mean: float = 0.0, std: float = 1.0, offset: int = 0):
     """Fill ``t`` (bf16 or fp32, contiguous) with the seeded synthetic stream."""
     assert t.is_contiguous()

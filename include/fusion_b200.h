@@ -348,6 +348,69 @@ int fus_ep_pack(const void* x, long ldx, int H, const int* send_ids, int n, int 
 int fus_ep_unpack(const void* rows, long ldr, int H, const int* send_ids, int n, void* y, long ldy,
                   void* stream, int* status);
 
+/* Row exchange over NVLink peer memory for the fixed-slot (decode) step, replacing the
+ * three all_to_alls with direct peer stores and flag waits. Every rank exports one
+ * exchange buffer through CUDA IPC and maps the others':
+ *   recv_rows [W*S][H] bf16 (block w: rows from rank w), recv_leid [W*S] int32 (-1 =
+ *   unused slot), ret_rows [W*S][H] bf16 (block d: expert rows returned by rank d),
+ *   dflags [W], cflags [W] int32 (zero before the first step), epoch (int, zero).
+ * peer_* arguments are device arrays of W addresses (rank w's buffer at index w, this
+ * rank's own included).
+ * fus_ep_p2p_dispatch: epoch += 1; pair (t, k) whose owner is d, j-th of this rank's
+ *   pairs to d: recv_rows_d[rank*S + j] = x[t], recv_leid_d[rank*S + j] = local expert
+ *   (others of the block -1), slot_of_pair[t*topk + k] = d*S + j; then dflags_d[rank] =
+ *   epoch at every d (release, system scope). T*topk <= min(S, 1024).
+ * fus_ep_p2p_wait: until flags[w] >= epoch for every w; after timeout_ns (0 = 1 s,
+ *   the maximum) sets FUS_ERR_TIMEOUT in *status and returns.
+ * fus_ep_p2p_combine: for every live slot i = w*S + j of recv_leid:
+ *   ret_rows_w[rank*S + j] = y[i]; then cflags_w[rank] = epoch at every w.
+ * The merge then reads row (t, k) at ret_rows[slot_of_pair[t*topk + k]]
+ * (fus_merge_pos). fus_ipc_handle / fus_ipc_open / fus_ipc_close wrap CUDA IPC for an
+ * address inside any device allocation (handle = 64 bytes + the offset from the
+ * allocation's base). */
+int fus_ipc_handle(const void* ptr, void* handle_out, size_t* offset_out);
+int fus_ipc_open(const void* handle, size_t offset, void** ptr_out);
+int fus_ipc_close(void* ptr, size_t offset);
+int fus_ep_p2p_dispatch(const void* x, long ldx, int H, const int* topi, int T, int topk,
+                        int E_loc, int W, int S, int rank, const unsigned long long* peer_rows,
+                        const unsigned long long* peer_leid,
+                        const unsigned long long* peer_flags, int* epoch, int* slot_of_pair,
+                        void* stream, int* status);
+int fus_ep_p2p_wait(const int* flags, const int* epoch, int W, unsigned long long timeout_ns,
+                    void* stream, int* status);
+int fus_ep_p2p_combine(const void* y, long ldy, int H, const int* recv_leid, int W, int S,
+                       int rank, const unsigned long long* peer_ret,
+                       const unsigned long long* peer_cflags, const int* epoch, void* stream,
+                       int* status);
+
+/* The whole expert-parallel decode step of one rank over the NVLink exchange, as seven
+ * launches chained with programmatic dependent launch: fused norm + router + top-k,
+ * dispatch, [wait for every source + layout of the received slots], w13 + SwiGLU
+ * (received rows gathered, shared expert as a second group), w2, combine, [wait for
+ * every owner + merge]. blk->E counts all experts and blk->w13 / w2 hold this rank's
+ * E_loc = E / W experts; S >= T*topk; the exchange buffers as described above.
+ * Requires the fused front end (E <= 256, E even, T*topk <= 256). The workspace must be
+ * zeroed before its first use (a front-end ticket that each call leaves at zero). */
+typedef struct fus_ep_p2p_desc {
+  const fus_moe_block_desc* blk;
+  int E_loc, W, rank, S;
+  const unsigned long long* peer_rows;    /* [W] every rank's recv_rows   */
+  const unsigned long long* peer_leid;    /* [W] every rank's recv_leid   */
+  const unsigned long long* peer_dflags;  /* [W] every rank's dflags      */
+  const unsigned long long* peer_ret;     /* [W] every rank's ret_rows    */
+  const unsigned long long* peer_cflags;  /* [W] every rank's cflags      */
+  void* recv_rows;                        /* this rank's buffers          */
+  int* recv_leid;
+  void* ret_rows;
+  int* dflags;
+  int* cflags;
+  int* epoch;
+} fus_ep_p2p_desc;
+size_t fus_ep_p2p_decode_workspace(const fus_ep_p2p_desc* d, int T);
+int fus_ep_p2p_decode_forward(const fus_ep_p2p_desc* d, const void* h, const void* r, int T,
+                              void* out, void* h1, float* topw, int* topi, void* workspace,
+                              size_t ws_bytes, void* stream, int* status);
+
 /* ---------------------------------------------------------------------------------
  * Seeded synthetic inputs, bit-identical on the GPU and the host (no reference
  * counterpart: the reference draws torch.randn on the device, which a CPU oracle

@@ -15,7 +15,8 @@ import torch
 
 from fusion_b200 import ops, synth
 from fusion_b200.block import MoEBlock
-from fusion_b200.ep import CudaEPBackend, EPDecodeGraph, ExpertParallelMoE, shard_weights
+from fusion_b200.ep import (CudaEPBackend, EPDecodeGraph, EPDecodeStep, ExpertParallelMoE,
+                            P2PExchange, shard_weights)
 from oracle import reference_np as O
 from gpu_util import DEV, finish
 
@@ -97,12 +98,52 @@ def test_ep_single_rank_matches_block(T, fixed):
     assert torch.equal(res["h1"].view(torch.int16), ref.h1.view(torch.int16))
     _parity(res["out"], ref.out)
     if fixed:
-        g = EPDecodeGraph(ep, T, D.H, DEV)
-        g.h.copy_(h)
-        g.r.copy_(r)
-        out = g.replay()
-        finish()
-        assert torch.equal(out.view(torch.int16), res["out"].view(torch.int16))
+        # the NVLink exchange (here its loopback on one rank) gives the same bits
+        x = P2PExchange(T * D.topk, D.H, DEV)
+        for _ in range(2):  # the second step reuses the buffers with the next epoch
+            res_p = ep.forward_p2p(h, r, x)
+            finish()
+            assert torch.equal(res_p["out"].view(torch.int16), res["out"].view(torch.int16))
+        x.close()
+        for exchange in ("nccl", "p2p"):
+            g = EPDecodeGraph(ep, T, D.H, DEV, exchange=exchange)
+            g.h.copy_(h)
+            g.r.copy_(r)
+            for _ in range(2):
+                out = g.replay()
+                finish()
+                assert torch.equal(out.view(torch.int16), res["out"].view(torch.int16))
+            if g.x is not None:
+                g.x.close()
+        # the whole step as one library call (PDL-chained launches), eager and graphed
+        st = EPDecodeStep(be, T)
+        st.h.copy_(h)
+        st.r.copy_(r)
+        for _ in range(2):
+            out = st.forward()
+            finish()
+            assert torch.equal(out.view(torch.int16), res["out"].view(torch.int16))
+        st.capture()
+        for _ in range(2):
+            out = st.replay()
+            finish()
+            assert torch.equal(out.view(torch.int16), res["out"].view(torch.int16))
+        assert torch.equal(st.topi, res["topi"])
+        st.close()
+
+
+def test_p2p_wait_times_out_with_status():
+    """A flag that nothing raises: the bounded wait gives up and reports FUS_ERR_TIMEOUT;
+    the context stays usable."""
+    flags = torch.zeros(2, dtype=torch.int32, device=DEV)
+    epoch = torch.ones(1, dtype=torch.int32, device=DEV)
+    ops.read_status()
+    ops.ep_p2p_wait(flags, epoch, 2, timeout_ns=20_000_000)  # 20 ms
+    assert ops.read_status() & ops.ERR_TIMEOUT
+    flags.fill_(1)
+    ops.ep_p2p_wait(flags, epoch, 2, timeout_ns=20_000_000)
+    assert ops.read_status() == 0
+    finish()
 
 
 def _two_rank_worker(rank, port, q):
@@ -121,14 +162,29 @@ def _two_rank_worker(rank, port, q):
         h, r = synth.make_inputs(70 + rank, 24, D, "cuda")
         out = ep(h, r)["out"]
         h2, r2 = synth.make_inputs(90 + rank, 2, D, "cuda")
-        g = EPDecodeGraph(ep, 2, D.H, "cuda")  # fixed-slot step in a CUDA graph
+        g = EPDecodeGraph(ep, 2, D.H, "cuda", exchange="nccl")  # all_to_all in a CUDA graph
         g.h.copy_(h2)
         g.r.copy_(r2)
         out2 = g.replay()
+        gp = EPDecodeGraph(ep, 2, D.H, "cuda", exchange="p2p")  # NVLink peer stores
+        gp.h.copy_(h2)
+        gp.r.copy_(r2)
+        for _ in range(3):
+            out3 = gp.replay()
+        st = EPDecodeStep(be, 2).capture()  # one library call per step, graphed
+        st.h.copy_(h2)
+        st.r.copy_(r2)
+        for _ in range(3):
+            out4 = st.replay()
         torch.cuda.synchronize()
-        q.put((rank, (out.float().cpu().numpy(), out2.float().cpu().numpy())))
+        ops.check_status()
+        same = bool(torch.equal(out2.view(torch.int16), out3.view(torch.int16)) and
+                    torch.equal(out2.view(torch.int16), out4.view(torch.int16)))
+        q.put((rank, (out.float().cpu().numpy(), out2.float().cpu().numpy(), same)))
         del g  # the graph holds NCCL work: release it before the communicator
         torch.cuda.synchronize()
+        gp.x.close()
+        st.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -156,7 +212,8 @@ def test_ep_two_nccl_ranks_match_block():
     w = synth.make_block_weights(404, D, DEV)
     blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"])
     for rank in range(2):
-        for (seed, T), got in zip(((70, 24), (90, 2)), outs[rank]):
+        assert outs[rank][2], "NVLink exchange differs from the all_to_all exchange"
+        for (seed, T), got in zip(((70, 24), (90, 2)), outs[rank][:2]):
             h, r = synth.make_inputs(seed + rank, T, D, DEV)
             ref = blk(h, r)
             finish()

@@ -118,6 +118,8 @@ SIGNATURES: dict[str, tuple] = {
     "fus_router_nsplit": (i32, [i32, i32, i32, i32]),
     "fus_router_logits": (i32, [vp, i64, vp, i32, vp, i32, i32, i32, i32, vp, vp]),
     "fus_router_topk": (i32, [vp, i32, vp, vp, vp, vp, i32, i32, i32, f32, i32, vp, vp]),
+    "fus_router_topk_grouped": (i32, [vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp,
+                                      vp]),
     "fus_moe_align_workspace": (sz, [i32, i32]),
     "fus_moe_align": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, sz, vp, vp]),
     "fus_moe_align_ex": (i32, [vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, i32, vp, sz, vp, vp]),

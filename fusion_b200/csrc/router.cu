@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32)
     topk_kernel(const float* __restrict__ partial, long split_stride, int nsplit,
                 const float* __restrict__ bias, float* __restrict__ logits_out,
                 float* __restrict__ topw, int* __restrict__ topi, int T, int E, int topk,
-                float scale, int renorm) {
+                float scale, int renorm, int n_group, int topk_group) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * kTopkWarps + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -89,6 +89,43 @@ __global__ void __launch_bounds__(kTopkWarps * 32)
     } else {
       sc[j] = 0.f;
       ch[j] = -INFINITY;
+    }
+  }
+  if (n_group > 1) {
+    // noaux_tc group masking (reference.py:159-166): group score = sum of the group's two
+    // largest choice values; experts outside the topk_group best groups get choice * 0
+    // (0 or -0, as the reference's multiply by the 0/1 mask). A group of gs = E/n_group
+    // consecutive experts spans gs/8 consecutive lanes (gs % 8 == 0, host check).
+    float a1 = -INFINITY, a2 = -INFINITY;  // this lane's two largest
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = ch[j];
+      if (v > a1) {
+        a2 = a1;
+        a1 = v;
+      } else if (v > a2) {
+        a2 = v;
+      }
+    }
+    const int lpg = (E / n_group) >> 3;  // lanes per group (a power of two here)
+    for (int o = 1; o < lpg; o <<= 1) {  // merge the top-2 of lane pairs within a group
+      const float b1 = __shfl_xor_sync(0xffffffffu, a1, o);
+      const float b2 = __shfl_xor_sync(0xffffffffu, a2, o);
+      const float hi = fmaxf(a1, b1);
+      const float lo = fmaxf(fminf(a1, b1), fmaxf(a2, b2));
+      a1 = hi;
+      a2 = lo;
+    }
+    const float gscore = a1 + a2;  // the reference sums its descending top-2 values
+    const int my_g = lane / lpg;
+    int better = 0;  // groups ranked ahead of mine (score, then lower group index)
+    for (int g = 0; g < n_group; ++g) {
+      const float og = __shfl_sync(0xffffffffu, gscore, g * lpg);
+      better += (og > gscore) || (og == gscore && g < my_g);
+    }
+    if (e0 < E && better >= topk_group) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ch[j] = ch[j] * 0.0f;
     }
   }
   unsigned used = 0;
@@ -288,10 +325,17 @@ extern "C" int fus_router_logits(const void* x2, long ldx, const void* wa, int n
                           status);
 }
 
-extern "C" int fus_router_topk(const float* partial, int nsplit, const float* bias,
-                               float* logits_out, float* topw, int* topi, int T, int E, int topk,
-                               float scale, int renorm, void* stream, int* status) {
+extern "C" int fus_router_topk_grouped(const float* partial, int nsplit, const float* bias,
+                                       float* logits_out, float* topw, int* topi, int T, int E,
+                                       int topk, int n_group, int topk_group, float scale,
+                                       int renorm, void* stream, int* status) {
   (void)status;
+  if (n_group < 1 || topk_group < 1 || topk_group > n_group || E % n_group ||
+      (n_group > 1 && ((E / n_group) % 8 || ((E / n_group / 8) & (E / n_group / 8 - 1)) ||
+                       n_group > 32 || topk > topk_group * (E / n_group))))
+    return set_error(FUS_E_UNSUPPORTED,
+                     "router_topk: n_group=%d topk_group=%d E=%d (groups of 8*2^k experts, "
+                     "n_group <= 32)", n_group, topk_group, E);
   if (!partial || !topw || !topi || T < 0 || nsplit < 1)
     return set_error(FUS_E_INVALID, "router_topk: bad args");
   if (E <= 0 || E > 256 || E % 8 || topk < 1 || topk > 16 || topk > E)
@@ -300,6 +344,14 @@ extern "C" int fus_router_topk(const float* partial, int nsplit, const float* bi
     return set_error(FUS_E_INVALID, "router_topk: logits must be 16-byte aligned");
   if (T == 0) return FUS_OK;
   topk_kernel<<<ceil_div(T, kTopkWarps), kTopkWarps * 32, 0, as_stream(stream)>>>(
-      partial, (long)T * E, nsplit, bias, logits_out, topw, topi, T, E, topk, scale, renorm);
+      partial, (long)T * E, nsplit, bias, logits_out, topw, topi, T, E, topk, scale, renorm,
+      n_group, topk_group);
   return check_launch("router_topk");
+}
+
+extern "C" int fus_router_topk(const float* partial, int nsplit, const float* bias,
+                               float* logits_out, float* topw, int* topi, int T, int E, int topk,
+                               float scale, int renorm, void* stream, int* status) {
+  return fus_router_topk_grouped(partial, nsplit, bias, logits_out, topw, topi, T, E, topk, 1, 1,
+                                 scale, renorm, stream, status);
 }

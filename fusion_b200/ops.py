@@ -101,11 +101,16 @@ def router_logits(x2, wa, nplanes: int, partial, nsplit: int):
 
 
 def router_topk(partial, nsplit: int, bias, logits_out, topw, topi, scale: float = 2.5,
-                renorm: bool = True):
+                renorm: bool = True, n_group: int = 1, topk_group: int = 1):
     T, topk = topi.shape
     E = partial.shape[-1]
-    L.call("fus_router_topk", _p(partial), nsplit, _p(bias), _p(logits_out), _p(topw), _p(topi),
-           T, E, topk, scale, int(renorm), _stream(), _sp())
+    if n_group == 1:
+        L.call("fus_router_topk", _p(partial), nsplit, _p(bias), _p(logits_out), _p(topw),
+               _p(topi), T, E, topk, scale, int(renorm), _stream(), _sp())
+    else:
+        L.call("fus_router_topk_grouped", _p(partial), nsplit, _p(bias), _p(logits_out),
+               _p(topw), _p(topi), T, E, topk, n_group, topk_group, scale, int(renorm),
+               _stream(), _sp())
 
 
 def moe_align_workspace(numel: int, E: int) -> int:

@@ -103,6 +103,15 @@ int fus_router_logits(const void* x2, long ldx, const void* wa, int nplanes, flo
 int fus_router_topk(const float* partial, int nsplit, const float* bias, float* logits_out,
                     float* topw, int* topi, int T, int E, int topk, float scale, int renorm,
                     void* stream, int* status);
+/* Same with noaux_tc group masking (reference.py:159-166, DeepSeek-V3-style configs):
+ * experts form n_group groups of E/n_group consecutive ids; a group's score is the sum
+ * of its two largest choice values; experts outside the topk_group best groups (ties:
+ * lower group index) get choice * 0 before the top-k. Groups of 8*2^j experts,
+ * n_group <= 32. n_group = 1 is fus_router_topk (GLM-5.2). */
+int fus_router_topk_grouped(const float* partial, int nsplit, const float* bias,
+                            float* logits_out, float* topw, int* topi, int T, int E, int topk,
+                            int n_group, int topk_group, float scale, int renorm, void* stream,
+                            int* status);
 
 /* ---------------------------------------------------------------------------------
  * Dispatch layout (glm52/reference.py:85-128 moe_align_block_size, sglang layout):

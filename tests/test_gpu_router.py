@@ -63,6 +63,34 @@ def test_router_golden():
     check_ids(ti0, g["topk_ids_nobias"], g["logits_nobias"], None)
 
 
+def test_router_grouped_golden():
+    """noaux_tc group masking (n_group=8, topk_group=4) on the reference's own logits:
+    ids bit-exact against its golden ids, weights to fp32 rounding; and against the
+    oracle on fresh logits at several T (ties between groups / experts are rare but the
+    oracle breaks them by lower index exactly like the kernel)."""
+    g = golden("router")
+    T = int(g["T"])
+    bias = synth.make("bias", (256,), int(g["seed"]), DEV)
+    part = torch.from_numpy(g["logits"]).to(DEV).view(1, T, 256).contiguous()
+    tw = torch.empty(T, 8, dtype=torch.float32, device=DEV)
+    ti = torch.empty(T, 8, dtype=torch.int32, device=DEV)
+    ops.router_topk(part, 1, bias, None, tw, ti, n_group=8, topk_group=4)
+    finish()
+    assert np.array_equal(np.sort(ti.cpu().numpy(), 1), np.sort(g["topk_ids_grouped"], 1))
+    assert np.array_equal(ti.cpu().numpy(), g["topk_ids_grouped"])
+    np.testing.assert_allclose(tw.cpu().numpy(), g["topk_weights_grouped"], rtol=2e-6, atol=1e-7)
+    for Tn, (ng, tg) in ((1, (8, 4)), (77, (8, 4)), (300, (4, 2)), (64, (32, 3))):
+        lg = synth.make("r", (Tn, 256), 5 + Tn, "cpu").float().numpy() * 3.0
+        pt = torch.from_numpy(lg).to(DEV).view(1, Tn, 256).contiguous()
+        tw = torch.empty(Tn, 8, dtype=torch.float32, device=DEV)
+        ti = torch.empty(Tn, 8, dtype=torch.int32, device=DEV)
+        ops.router_topk(pt, 1, bias, None, tw, ti, n_group=ng, topk_group=tg)
+        finish()
+        ow, oi = O.router_select(lg, to_np(bias), n_group=ng, topk_group=tg)
+        assert np.array_equal(ti.cpu().numpy(), oi), (Tn, ng, tg)
+        np.testing.assert_allclose(tw.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+
+
 @pytest.mark.parametrize("T", [1, 33, 256, 2048])
 def test_router_vs_oracle(T):
     x2 = synth.make("h", (T, 6144), 21 + T, DEV)

@@ -38,6 +38,8 @@ class GemmGroup(C.Structure):
         ("token_div", i32),
         ("gather_ids", vp),
         ("gather_div", i32),
+        ("res", vp),
+        ("ldr", i64),
     ]
 
 
@@ -159,6 +161,12 @@ SIGNATURES: dict[str, tuple] = {
     "fus_ep_p2p_wait": (i32, [vp, vp, i32, u64, vp, vp]),
     "fus_ep_p2p_combine": (i32, [vp, i64, i32, vp, i32, i32, i32, vp, vp, vp, vp, vp]),
     "fus_ep_p2p_decode_workspace": (sz, [vp, i32]),
+    "fus_oproj_workspace": (sz, [i32, i32, i32, i32]),
+    "fus_oproj_resadd": (i32, [vp, i64, vp, i32, i32, i32, vp, i64, vp, i64, i32, vp, sz, vp, vp]),
+    "fus_oproj_f32_workspace": (sz, [i32, i32, i32]),
+    "fus_oproj_gemm_f32": (i32, [vp, i64, vp, i32, i32, i32, vp, i64, vp, i64, i32, vp, sz, vp,
+                                 vp]),
+    "fus_oproj_finish": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, vp, vp]),
     "fus_ep_p2p_decode_forward": (i32, [vp, vp, vp, i32, vp, vp, vp, vp, vp, sz, vp, vp]),
     "fus_synth_fill": (i32, [vp, i32, i64, i64, u64, f32, f32, vp]),
     "fus_synth_fill_host": (None, [vp, i32, i64, i64, u64, f32, f32]),

@@ -40,6 +40,8 @@ struct GroupDev {
   const int* gather_ids;
   int gather_div;
   int tma_store;  // persistent kernel: dense output written by TMA tile stores
+  const __nv_bfloat16* res;  // optional residual (FUS_EPI_BF16), row stride ldr
+  long ldr;
 };
 
 struct MergeDev {
@@ -450,6 +452,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float sc = G.row_scale ? __ldg(G.row_scale + row) : 1.0f;
 #pragma unroll
               for (int e = 0; e < 8; ++e) vv[e] *= sc;
+              if (G.res) {
+                float rr[8];
+                unpack8(__ldg(reinterpret_cast<const uint4*>(G.res + (long)row * G.ldr + col0 +
+                                                             q * 8)), rr);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) vv[e] += rr[e];
+              }
               if (G.flags & FUS_GEMM_OUT_F32) {
                 float4* dp = reinterpret_cast<float4*>(reinterpret_cast<float*>(G.out) +
                                                        (long)row * G.ldo + col0 + q * 8);
@@ -724,6 +733,11 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
     D.token_div = G.token_div > 0 ? G.token_div : 1;
     D.gather_ids = G.gather_ids;
     D.gather_div = G.gather_div > 0 ? G.gather_div : 1;
+    if (G.res && (epilogue != FUS_EPI_BF16 || (G.flags & FUS_GEMM_MERGE) || G.ldr % 8 ||
+                  !aligned16(G.res)))
+      return set_error(FUS_E_INVALID, "group %d: residual needs FUS_EPI_BF16, 16-byte rows", g);
+    D.res = reinterpret_cast<const __nv_bfloat16*>(G.res);
+    D.ldr = G.ldr;
     units[g] = (long)G.max_blocks * a.m_tiles * a.ksplit;
   }
   if (ngroups == 1) {

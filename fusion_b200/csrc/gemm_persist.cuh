@@ -343,6 +343,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 v[j] *= row < G.row_limit ? __ldg(G.row_scale + row) : 0.f;
               }
             }
+            if (EPI != FUS_EPI_SWIGLU && G.res) {  // residual of feature col0 + m
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int pos = pos0 + c0 + c + j;
+                const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
+                if (row < G.row_limit)
+                  v[j] += __bfloat162float(G.res[(long)row * G.ldr + col0 + m]);
+              }
+            }
             if (out32) {
               float* st = reinterpret_cast<float*>(stg);
 #pragma unroll

@@ -45,6 +45,12 @@ int merge_pos_after_flags(const void* y, long ldy, const int* pos_of, int K, con
                           int extra_f32, void* out, long ldo, int T, int H, const int* flags,
                           const int* epoch, int W, int pdl, void* stream, int* status);
 
+// o_proj split-K finish: out = bf16(sum of S fp32 planes (bf16-rounded if round_mid) + res)
+// (out_f32: out is fp32, += when accumulate)
+int oproj_finish(const float* part, long plane, int S, long ldp, const void* res, long ldr,
+                 void* out, long ldo, int T, int N, int round_mid, void* stream,
+                 int out_f32 = 0, int accumulate = 0);
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }

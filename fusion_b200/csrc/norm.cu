@@ -172,6 +172,53 @@ __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, lon
   *reinterpret_cast<uint4*>(out + (long)t * ldo + c) = pack8(acc);
 }
 
+// o_proj split-K finish (glm52/kernels/oproj_resadd.py epilogue_kernel; bench_layer.py:355):
+//   out = bf16(sum_s part[s] (+ res))          fused: one rounding
+//   out = bf16(bf16(sum_s part[s]) + res)      round_mid: the unfused chain's c, then add
+// out32 (optional): fp32 result instead, += when accumulate (the reference's atomic acc32)
+__global__ void oproj_finish_kernel(const float* __restrict__ part, long plane, int S, long ldp,
+                                    const __nv_bfloat16* __restrict__ res, long ldr,
+                                    __nv_bfloat16* __restrict__ out, long ldo, int N,
+                                    int round_mid, float* __restrict__ out32, int accumulate) {
+  const int t = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= N) return;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int s = 0; s < S; ++s) {
+    const float* p = part + (long)s * plane + (long)t * ldp + c;
+    const uint4 a = ldg_stream(p);
+    const uint4 b = ldg_stream(p + 4);
+    acc[0] += __uint_as_float(a.x); acc[1] += __uint_as_float(a.y);
+    acc[2] += __uint_as_float(a.z); acc[3] += __uint_as_float(a.w);
+    acc[4] += __uint_as_float(b.x); acc[5] += __uint_as_float(b.y);
+    acc[6] += __uint_as_float(b.z); acc[7] += __uint_as_float(b.w);
+  }
+  if (round_mid) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = round_bf(acc[e]);
+  }
+  if (res) {
+    float r[8];
+    unpack8(ldg_stream(res + (long)t * ldr + c), r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += r[e];
+  }
+  if (out32) {
+    float4* o = reinterpret_cast<float4*>(out32 + (long)t * ldo + c);
+    if (accumulate) {
+      const float4 a = o[0], b = o[1];
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    return;
+  }
+  *reinterpret_cast<uint4*>(out + (long)t * ldo + c) = pack8(acc);
+}
+
 __global__ void add_kernel(const __nv_bfloat16* __restrict__ a, long lda,
                            const __nv_bfloat16* __restrict__ b, long ldb,
                            __nv_bfloat16* __restrict__ o, long ldo, int N) {
@@ -288,6 +335,16 @@ extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float
 }
 
 namespace fus {
+int oproj_finish(const float* part, long plane, int S, long ldp, const void* res, long ldr,
+                 void* out, long ldo, int T, int N, int round_mid, void* stream, int out_f32,
+                 int accumulate) {
+  if (T == 0) return FUS_OK;
+  oproj_finish_kernel<<<row_grid(T, N, 128), 128, 0, as_stream(stream)>>>(
+      part, plane, S, ldp, (const bf16*)res, ldr, out_f32 ? nullptr : (bf16*)out, ldo, N,
+      round_mid, out_f32 ? (float*)out : nullptr, accumulate);
+  return check_launch("oproj_finish");
+}
+
 int merge_pos_after_flags(const void* y, long ldy, const int* pos_of, int K, const float* w,
                           long ldw, const void* res, long ldr, const void* extra, long lde,
                           int extra_f32, void* out, long ldo, int T, int H, const int* flags,

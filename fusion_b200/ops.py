@@ -163,7 +163,8 @@ def permute_rows(src, sorted_ids, ntp, div: int, num_valid: int, dst, max_rows: 
 def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map=None,
                row_limit: int, row_scale=None, x_rows: int | None = None,
                flags: int = 0, live_ids=None, live_limit: int = 0,
-               token_div: int = 1, gather_ids=None, gather_div: int = 1) -> L.GemmGroup:
+               token_div: int = 1, gather_ids=None, gather_div: int = 1,
+               res=None) -> L.GemmGroup:
     """Describe one weight stack + token rows for :func:`grouped_gemm`.
 
     ``w`` is [n_experts, w_rows, K'] (or [w_rows, K'] for one expert) bf16."""
@@ -187,6 +188,8 @@ def gemm_group(w, x, out, *, expert_ids=None, ntp=None, max_blocks: int, row_map
     g.token_div = token_div
     g.gather_ids = _p(gather_ids)
     g.gather_div = gather_div
+    g.res = _p(res)
+    g.ldr = _ld(res) if res is not None else 0
     return g
 
 
@@ -249,6 +252,19 @@ def merge_pos(y, pos_of, K: int, w, res, extra, out):
            _p(extra), _ld(extra) if extra is not None else 0,
            int(extra is not None and extra.dtype == torch.float32), _p(out), _ld(out), T, H,
            _stream(), _sp())
+
+
+def oproj_resadd(a, w_nk, res, out, fuse: bool = True, workspace=None):
+    """out = bf16(a @ w_nk.T + res) (fuse) or bf16(bf16(a @ w_nk.T) + res); w_nk is the
+    K-major [N, K] weight."""
+    T, K = a.shape
+    N = w_nk.shape[0]
+    need = int(L.lib().fus_oproj_workspace(T, N, K, int(fuse)))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
+    L.call("fus_oproj_resadd", _p(a), _ld(a), _p(w_nk), T, N, K, _p(res),
+           _ld(res) if res is not None else 0, _p(out), _ld(out), int(fuse), _p(workspace),
+           need, _stream(), _sp())
 
 
 def add(a, b, o):

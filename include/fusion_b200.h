@@ -224,6 +224,8 @@ typedef struct fus_gemm_group {
   const int* gather_ids;  /* optional: token rows are gathered, not read densely: row j of */
   int gather_div;         /*   block b is x[gather_ids[b*block_n+j] / gather_div] when that */
                           /*   id is live (< live_limit), zeros otherwise (TMA gather4)     */
+  const void* res;        /* optional, FUS_EPI_BF16: bf16 residual added before the output */
+  long ldr;               /*   rounding, out[r, n] = bf16(acc + res[r, n]) (o_proj+ResAdd)  */
 } fus_gemm_group;
 
 int fus_grouped_gemm(const fus_gemm_group* groups, int ngroups, int w_rows, int K, int a_kplanes,
@@ -265,6 +267,30 @@ typedef struct fus_merge_spec {
 int fus_grouped_gemm_tiles(int w_rows, int epilogue, int block_n);
 int fus_grouped_gemm_merge(const fus_gemm_group* groups, int ngroups, int w_rows, int K,
                            int block_n, const fus_merge_spec* merge, void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
+ * o_proj GEMM + ResAdd1 (glm52/kernels/oproj_resadd.py:144 gemm_launch / :181
+ * epilogue_launch / :199 make_fused_chain / :216 make_unfused_chain;
+ * glm52/bench/bench_layer.py:399-415):
+ *   fuse = 1: out = bf16(a @ W + res)            (fp32 sum, one rounding)
+ *   fuse = 0: out = bf16(bf16(a @ W) + res)      (the unfused chain's c, then the add)
+ * a [T, K] bf16 (row stride lda), W K-major [N, K] bf16 (the reference's w_o [K, N]
+ * transposed once), res [T, N] bf16 or NULL. N % 128 == 0, K % 64 == 0. T <= 64 splits K
+ * into fp32 partial planes summed in fixed order (deterministic). The workspace size
+ * comes from fus_oproj_workspace. */
+size_t fus_oproj_workspace(int T, int N, int K, int fuse);
+int fus_oproj_resadd(const void* a, long lda, const void* w, int T, int N, int K, const void* res,
+                     long ldr, void* out, long ldo, int fuse, void* workspace, size_t ws_bytes,
+                     void* stream, int* status);
+/* The reference's split-K form with an fp32 accumulator (gemm_launch atomic_out=True and
+ * epilogue_launch over acc32): fus_oproj_gemm_f32: acc32 (+)= a @ W (+ res) (+= when
+ * accumulate); fus_oproj_finish: out = bf16(acc32 (+ res)). */
+size_t fus_oproj_f32_workspace(int T, int N, int K);
+int fus_oproj_gemm_f32(const void* a, long lda, const void* w, int T, int N, int K,
+                       const void* res, long ldr, float* acc32, long ldc, int accumulate,
+                       void* workspace, size_t ws_bytes, void* stream, int* status);
+int fus_oproj_finish(const float* acc32, long ldc, const void* res, long ldr, void* out, long ldo,
+                     int T, int N, void* stream, int* status);
 
 /* ---------------------------------------------------------------------------------
  * Element-wise / merge kernels

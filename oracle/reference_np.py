@@ -226,3 +226,18 @@ def moe_block_exact_fp32(x2, h1, topk_weights, topk_ids, get_w13, get_w2, w13_s,
     if w13_s is not None:
         acc = acc + shared_expert_mlp_exact_fp32(x2, w13_s, w2_s)
     return acc.astype(np.float32)
+
+
+# ---------------------------------------------------------------------------------
+# o_proj + ResAdd1  (glm52/bench/bench_layer.py:355; glm52/kernels/oproj_resadd.py)
+# ---------------------------------------------------------------------------------
+def oproj_resadd(a: np.ndarray, w_kn: np.ndarray, residual, fused: bool = True) -> np.ndarray:
+    """h1 for attention output a [T, K] and o_proj weight w_kn [K, N] (bf16 values):
+    fused (bench_layer.py:355, oproj_resadd.py FUSE_RESADD): bf16(a @ w + residual) in fp32;
+    unfused without split-K (oproj_resadd.py:216-221): c = bf16(a @ w), h1 = bf16(c + residual)."""
+    acc = a.astype(np.float32) @ w_kn.astype(np.float32)
+    if not fused:
+        acc = bf16(acc)
+    if residual is not None:
+        acc = acc + residual.astype(np.float32)
+    return bf16(acc)

@@ -167,6 +167,9 @@ SIGNATURES: dict[str, tuple] = {
     "fus_oproj_gemm_f32": (i32, [vp, i64, vp, i32, i32, i32, vp, i64, vp, i64, i32, vp, sz, vp,
                                  vp]),
     "fus_oproj_finish": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, vp, vp]),
+    "fus_row_rstd": (i32, [vp, i64, i32, i32, f32, vp, vp, vp]),
+    "fus_fold_weight": (i32, [vp, vp, vp, i64, i32, i32, i64, vp, vp]),
+    "fus_scale_sum_planes": (i32, [vp, i32, i64, i32, i32, vp, vp, i64, vp, vp]),
     "fus_ep_p2p_decode_forward": (i32, [vp, vp, vp, i32, vp, vp, vp, vp, vp, sz, vp, vp]),
     "fus_synth_fill": (i32, [vp, i32, i64, i64, u64, f32, f32, vp]),
     "fus_synth_fill_host": (None, [vp, i32, i64, i64, u64, f32, f32]),

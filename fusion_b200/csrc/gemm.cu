@@ -449,7 +449,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               continue;
             }
             if (EPI == FUS_EPI_BF16) {
-              const float sc = G.row_scale ? __ldg(G.row_scale + row) : 1.0f;
+              const float sc =
+                  G.row_scale
+                      ? __ldg(G.row_scale + ((G.flags & FUS_GEMM_SCALE_TOKEN) ? row / G.token_div
+                                                                              : row))
+                      : 1.0f;
 #pragma unroll
               for (int e = 0; e < 8; ++e) vv[e] *= sc;
               if (G.res) {

@@ -340,7 +340,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
               for (int j = 0; j < 16; ++j) {
                 const int pos = pos0 + c0 + c + j;
                 const int row = G.row_map ? __ldg(G.row_map + pos) : pos;
-                v[j] *= row < G.row_limit ? __ldg(G.row_scale + row) : 0.f;
+                const int si = (G.flags & FUS_GEMM_SCALE_TOKEN) ? row / G.token_div : row;
+                v[j] *= row < G.row_limit ? __ldg(G.row_scale + si) : 0.f;
               }
             }
             if (EPI != FUS_EPI_SWIGLU && G.res) {  // residual of feature col0 + m

@@ -49,7 +49,7 @@ int merge_pos_after_flags(const void* y, long ldy, const int* pos_of, int K, con
 // (out_f32: out is fp32, += when accumulate)
 int oproj_finish(const float* part, long plane, int S, long ldp, const void* res, long ldr,
                  void* out, long ldo, int T, int N, int round_mid, void* stream,
-                 int out_f32 = 0, int accumulate = 0);
+                 int out_f32 = 0, int accumulate = 0, const float* row_scale = nullptr);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

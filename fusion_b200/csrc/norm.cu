@@ -179,7 +179,8 @@ __global__ void merge_kernel(const __nv_bfloat16* __restrict__ y, long ld_t, lon
 __global__ void oproj_finish_kernel(const float* __restrict__ part, long plane, int S, long ldp,
                                     const __nv_bfloat16* __restrict__ res, long ldr,
                                     __nv_bfloat16* __restrict__ out, long ldo, int N,
-                                    int round_mid, float* __restrict__ out32, int accumulate) {
+                                    int round_mid, float* __restrict__ out32, int accumulate,
+                                    const float* __restrict__ row_scale) {
   const int t = blockIdx.y;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c >= N) return;
@@ -194,6 +195,11 @@ __global__ void oproj_finish_kernel(const float* __restrict__ part, long plane, 
     acc[2] += __uint_as_float(a.z); acc[3] += __uint_as_float(a.w);
     acc[4] += __uint_as_float(b.x); acc[5] += __uint_as_float(b.y);
     acc[6] += __uint_as_float(b.z); acc[7] += __uint_as_float(b.w);
+  }
+  if (row_scale) {  // lazy pre-norm: the row's rstd applied after the contraction
+    const float rs = __ldg(row_scale + t);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= rs;
   }
   if (round_mid) {
 #pragma unroll
@@ -217,6 +223,47 @@ __global__ void oproj_finish_kernel(const float* __restrict__ part, long plane, 
     return;
   }
   *reinterpret_cast<uint4*>(out + (long)t * ldo + c) = pack8(acc);
+}
+
+// Lazy pre-norm pieces (glm52/kernels/lazy_prenorm.py:347 rstd_kernel, :75-86 fold_weight_*)
+// rstd[t] = 1 / sqrt(mean(x[t]^2) + eps), fp32 over the bf16 row; one CTA per row
+__global__ void __launch_bounds__(256)
+    row_rstd_kernel(const __nv_bfloat16* __restrict__ x, long ldx, int N, float eps,
+                    float* __restrict__ rstd) {
+  const int t = blockIdx.x;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 8; c < N; c += 256 * 8) {
+    float v[8];
+    unpack8(ldg_stream(x + (long)t * ldx + c), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+  }
+  __shared__ float red[8];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += red[w];
+    rstd[t] = 1.0f / sqrtf(s / (float)N + eps);
+  }
+}
+
+// dst[r, c] = bf16(src[r, c] * (by_row ? w[r] : w[c]))  (the affine norm weight folded
+// into a weight's K dimension: rows of a [K, N] weight, columns of an [.., N, K] one)
+__global__ void fold_weight_kernel(const __nv_bfloat16* __restrict__ src,
+                                   const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ dst, long rows, int cols,
+                                   int by_row, long wdiv) {
+  const long n = rows * (long)cols;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    const long r = i / cols;
+    const int c = (int)(i - r * cols);
+    const float s = __bfloat162float(w[by_row ? (r % wdiv) : c]);
+    dst[i] = __float2bfloat16_rn(__bfloat162float(src[i]) * s);
+  }
 }
 
 __global__ void add_kernel(const __nv_bfloat16* __restrict__ a, long lda,
@@ -337,11 +384,11 @@ extern "C" int fus_merge(const void* y, long ld_t, long ld_k, int K, const float
 namespace fus {
 int oproj_finish(const float* part, long plane, int S, long ldp, const void* res, long ldr,
                  void* out, long ldo, int T, int N, int round_mid, void* stream, int out_f32,
-                 int accumulate) {
+                 int accumulate, const float* row_scale) {
   if (T == 0) return FUS_OK;
   oproj_finish_kernel<<<row_grid(T, N, 128), 128, 0, as_stream(stream)>>>(
       part, plane, S, ldp, (const bf16*)res, ldr, out_f32 ? nullptr : (bf16*)out, ldo, N,
-      round_mid, out_f32 ? (float*)out : nullptr, accumulate);
+      round_mid, out_f32 ? (float*)out : nullptr, accumulate, row_scale);
   return check_launch("oproj_finish");
 }
 
@@ -364,6 +411,41 @@ extern "C" int fus_merge_pos(const void* y, long ldy, const int* pos_of, int K, 
   if (K > 0 && !pos_of) return set_error(FUS_E_INVALID, "merge_pos: pos_of is NULL");
   return merge_launch(y, 0, ldy, K, pos_of, w, ldw, res, ldr, extra, lde, extra_f32, out, ldo, T,
                       H, 0, stream);
+}
+
+extern "C" int fus_row_rstd(const void* x, long ldx, int T, int N, float eps, float* rstd,
+                            void* stream, int* status) {
+  (void)status;
+  if (!x || !rstd || T < 0 || N <= 0 || N % 8 || ldx % 8 || !aligned16(x))
+    return set_error(FUS_E_INVALID, "row_rstd: bad args");
+  if (T == 0) return FUS_OK;
+  row_rstd_kernel<<<T, 256, 0, as_stream(stream)>>>((const bf16*)x, ldx, N, eps, rstd);
+  return check_launch("row_rstd");
+}
+
+extern "C" int fus_fold_weight(const void* src, const void* w, void* dst, long rows, int cols,
+                               int by_row, long wdiv, void* stream, int* status) {
+  (void)status;
+  if (!src || !w || !dst || rows < 0 || cols <= 0 || (by_row && wdiv < 1))
+    return set_error(FUS_E_INVALID, "fold_weight: bad args");
+  const long n = rows * (long)cols;
+  if (n == 0) return FUS_OK;
+  long grid = (n + 255) / 256;
+  if (grid > 148L * 32) grid = 148L * 32;
+  fold_weight_kernel<<<(int)grid, 256, 0, as_stream(stream)>>>((const bf16*)src, (const bf16*)w,
+                                                               (bf16*)dst, rows, cols, by_row,
+                                                               by_row ? wdiv : 1);
+  return check_launch("fold_weight");
+}
+
+extern "C" int fus_scale_sum_planes(const float* partial, int nsplit, long plane, int T, int N,
+                                    const float* row_scale, float* out, long ldo, void* stream,
+                                    int* status) {
+  (void)status;
+  if (!partial || !out || T < 0 || N <= 0 || N % 8 || nsplit < 1 || ldo % 4)
+    return set_error(FUS_E_INVALID, "scale_sum_planes: bad args");
+  return oproj_finish(partial, plane, nsplit, N, nullptr, 0, out, ldo, T, N, 0, stream, 1, 0,
+                      row_scale);
 }
 
 extern "C" int fus_add(const void* a, long lda, const void* b, long ldb, void* o, long ldo, int M,

@@ -15,6 +15,7 @@ from . import _lib as L
 
 FUS_EPI_BF16, FUS_EPI_SWIGLU, FUS_EPI_F32 = 0, 1, 2
 GEMM_OUT_F32, GEMM_SWIGLU_EXACT, GEMM_W_STREAM, GEMM_MERGE, GEMM_NO_PERSIST = 0x1, 0x2, 0x4, 0x8, 0x10
+GEMM_SCALE_TOKEN = 0x20
 ERR_TIMEOUT, ERR_BAD_EXPERT, ERR_CAPACITY = 0x1, 0x2, 0x4
 
 _status: dict[int, torch.Tensor] = {}
@@ -265,6 +266,28 @@ def oproj_resadd(a, w_nk, res, out, fuse: bool = True, workspace=None):
     L.call("fus_oproj_resadd", _p(a), _ld(a), _p(w_nk), T, N, K, _p(res),
            _ld(res) if res is not None else 0, _p(out), _ld(out), int(fuse), _p(workspace),
            need, _stream(), _sp())
+
+
+def row_rstd(x, rstd, eps: float = 1e-5):
+    T, N = x.shape
+    L.call("fus_row_rstd", _p(x), _ld(x), T, N, eps, _p(rstd), _stream(), _sp())
+
+
+def fold_weight(src, w, dst, by_row: bool):
+    """dst = bf16(src * w) along K: rows of a [K, N] weight (by_row) or the last dim."""
+    if not (src.dtype == w.dtype == dst.dtype == torch.bfloat16):
+        raise TypeError("fold_weight: bf16 weight, norm weight and output required")
+    assert src.is_contiguous() and dst.is_contiguous()
+    cols = src.shape[-1]
+    rows = src.numel() // cols
+    L.call("fus_fold_weight", _p(src), _p(w), _p(dst), rows, cols, int(by_row),
+           src.shape[0] if by_row else 1, _stream(), _sp())
+
+
+def scale_sum_planes(partial, nsplit: int, row_scale, out):
+    T, N = out.shape
+    L.call("fus_scale_sum_planes", _p(partial), nsplit, T * N, T, N, _p(row_scale), _p(out),
+           _ld(out), _stream(), _sp())
 
 
 def add(a, b, o):

@@ -54,6 +54,8 @@ extern "C" {
                                   /* load it L2 evict-first (decode); default evict-normal */
 #define FUS_GEMM_MERGE 0x8        /* this group's rows take part in the fused merge of     */
                                   /* fus_grouped_gemm_merge (token = row / token_div)      */
+#define FUS_GEMM_SCALE_TOKEN 0x20 /* row_scale is indexed by token = row / token_div       */
+                                  /* (lazy pre-norm: the token's rstd), not by row          */
 #define FUS_GEMM_NO_PERSIST 0x10  /* (first group) keep one tile per CTA; by default wide- */
                                   /* tile launches with many tiles run one persistent CTA  */
                                   /* per SM that overlaps each epilogue with the next loads */
@@ -291,6 +293,24 @@ int fus_oproj_gemm_f32(const void* a, long lda, const void* w, int T, int N, int
                        void* workspace, size_t ws_bytes, void* stream, int* status);
 int fus_oproj_finish(const float* acc32, long ldc, const void* res, long ldr, void* out, long ldo,
                      int T, int N, void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
+ * Lazy pre-norm, half fused (F11b', glm52/kernels/lazy_prenorm.py): the affine RMSNorm
+ * weight w is folded into the next GEMM's K dimension once at load, the GEMM reads the
+ * un-normalised h1 and its output rows are scaled by rstd afterwards.
+ * fus_row_rstd: rstd[t] = 1/sqrt(mean_k x[t,k]^2 + eps)          (lazy_prenorm.py:347)
+ * fus_fold_weight: dst = bf16(src * w) along K: by_row = 1 scales row r of a [K, N]
+ *   weight by w[r % wdiv] (fold_weight_rowmajor), by_row = 0 scales column c of an
+ *   [.., N, K] weight by w[c] (fold_weight_nk)                      (lazy_prenorm.py:75-86)
+ * fus_scale_sum_planes: out[t, n] = row_scale[t] * sum_s partial[s, t, n] (fp32; the
+ *   router GEMM's partial planes with the rstd epilogue; row_scale may be NULL)
+ * The grouped GEMM applies a token's rstd with row_scale + FUS_GEMM_SCALE_TOKEN. */
+int fus_row_rstd(const void* x, long ldx, int T, int N, float eps, float* rstd, void* stream,
+                 int* status);
+int fus_fold_weight(const void* src, const void* w, void* dst, long rows, int cols, int by_row,
+                    long wdiv, void* stream, int* status);
+int fus_scale_sum_planes(const float* partial, int nsplit, long plane, int T, int N,
+                         const float* row_scale, float* out, long ldo, void* stream, int* status);
 
 /* ---------------------------------------------------------------------------------
  * Element-wise / merge kernels

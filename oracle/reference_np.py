@@ -241,3 +241,37 @@ def oproj_resadd(a: np.ndarray, w_kn: np.ndarray, residual, fused: bool = True) 
     if residual is not None:
         acc = acc + residual.astype(np.float32)
     return bf16(acc)
+
+
+# ---------------------------------------------------------------------------------
+# Lazy pre-norm, half fused  (glm52/kernels/lazy_prenorm.py; exact form reference.py:123)
+# ---------------------------------------------------------------------------------
+def row_rstd(x: np.ndarray, eps: float = RMS_NORM_EPS) -> np.ndarray:
+    """lazy_prenorm.py:347 rstd_kernel: 1/sqrt(mean(x^2) + eps) in fp32 per row."""
+    xf = x.astype(np.float32)
+    return (np.float32(1.0) / np.sqrt((xf * xf).mean(-1, dtype=np.float32) + np.float32(eps))
+            ).astype(np.float32)
+
+
+def fold_weight_rowmajor(b_kn: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """lazy_prenorm.py:75: B [K, N], row k scaled by w[k], rounded to bf16."""
+    return bf16(b_kn.astype(np.float32) * w.astype(np.float32)[:, None])
+
+
+def fold_weight_nk(bt: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """lazy_prenorm.py:80: B^T [..., N, K], column k scaled by w[k], rounded to bf16."""
+    return bf16(bt.astype(np.float32) * w.astype(np.float32))
+
+
+def lazy_router_logits(h: np.ndarray, b_folded_kn: np.ndarray, eps: float = RMS_NORM_EPS):
+    """The F11b' router: (h @ B_folded) * rstd(h), fp32."""
+    return ((h.astype(np.float32) @ b_folded_kn.astype(np.float32)) *
+            row_rstd(h, eps)[:, None]).astype(np.float32)
+
+
+def router_logits_exact_fp32(h: np.ndarray, w: np.ndarray, gate_w: np.ndarray,
+                             eps: float = RMS_NORM_EPS) -> np.ndarray:
+    """reference.py:123-132: (h * rstd * w) @ gate_w.T entirely in fp32."""
+    hf = h.astype(np.float32)
+    xn = hf * row_rstd(h, eps)[:, None] * w.astype(np.float32)
+    return (xn @ gate_w.astype(np.float32).T).astype(np.float32)

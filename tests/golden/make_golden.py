@@ -145,7 +145,20 @@ def gen_block_full():
                         out=bits(out), out_exact=f32(exact))
 
 
+def gen_lazy_prenorm():
+    """The reference's exact lazy-pre-norm router logits (reference.py:123,
+    router_logits_exact_fp32) at GLM dims; h, w, gate_w regenerated from the seed."""
+    T, seed = 8, 505
+    d = synth.Dims()
+    h = synth.make("h", (T, d.H), seed)
+    w = synth.make("gamma", (d.H,), seed)
+    gw = synth.make("gate_w", (d.E, d.H), seed)
+    lg = R.router_logits_exact_fp32(h, w, gw)
+    np.savez_compressed(HERE / "lazy_prenorm.npz", seed=seed, T=T, logits_exact=f32(lg))
+
+
 if __name__ == "__main__":
+    gen_lazy_prenorm()
     gen_addnorm()
     gen_router()
     gen_align()

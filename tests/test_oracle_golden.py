@@ -112,3 +112,19 @@ def test_full_block_t2_matches_reference():
     exact = O.moe_block_exact_fp32(res["x2"], res["h1"], res["topk_weights"], res["topk_ids"],
                                    get("w13"), get("w2"), w13s, w2s, d.E)
     np.testing.assert_allclose(exact, g["out_exact"], rtol=1e-4, atol=1e-4)
+
+
+def test_lazy_prenorm_exact_logits_match_reference():
+    """router_logits_exact_fp32 (reference.py:123) on the reference's own output; the
+    half-fused form (folded bf16 weight, rstd after the GEMM) stays within 2e-2 * rms."""
+    g = golden("lazy_prenorm")
+    seed, T = int(g["seed"]), int(g["T"])
+    d = synth.Dims()
+    h = synth.make("h", (T, d.H), seed).float().numpy()
+    w = synth.make("gamma", (d.H,), seed).float().numpy()
+    gw = synth.make("gate_w", (d.E, d.H), seed).float().numpy()
+    ex = O.router_logits_exact_fp32(h, w, gw)
+    np.testing.assert_allclose(ex, g["logits_exact"], rtol=0, atol=2e-5)
+    lz = O.lazy_router_logits(h, O.fold_weight_rowmajor(gw.T.copy(), w))
+    rms = float(np.sqrt((ex.astype(np.float64) ** 2).mean()))
+    assert float(np.abs(lz - ex).max()) <= 2e-2 * rms

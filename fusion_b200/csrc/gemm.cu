@@ -90,8 +90,12 @@ struct GemmCfg {
   static constexpr int A_BYTES = MT * kATileBytes;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // small tiles: ~110 KB so that two CTAs share an SM; otherwise ~200 KB
-  static constexpr int RING_TARGET = (MT == 1 && BN <= 64) ? 112 * 1024 : 200 * 1024;
+  // decode tiles (block_n <= 32): ~72 KB so that three CTAs share an SM (a w2 launch of
+  // 9 experts x 48 tiles then runs in one wave: 432 CTAs, 444 slots); block_n 64:
+  // ~110 KB, two per SM; otherwise ~200 KB. Bytes in flight per SM stay ~200 KB.
+  static constexpr int RING_TARGET = (MT == 1 && BN <= 32)   ? 72 * 1024
+                                     : (MT == 1 && BN <= 64) ? 112 * 1024
+                                                             : 200 * 1024;
   static constexpr int STAGES = RING_TARGET / STAGE_BYTES > 8 ? 8 : RING_TARGET / STAGE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = pow2_at_least(MT * BN < 32 ? 32 : MT * BN, 32);

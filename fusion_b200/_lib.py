@@ -168,6 +168,7 @@ SIGNATURES: dict[str, tuple] = {
                                  vp]),
     "fus_oproj_finish": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, vp, vp]),
     "fus_row_rstd": (i32, [vp, i64, i32, i32, f32, vp, vp, vp]),
+    "fus_fp8_block_dequant": (i32, [vp, vp, i64, vp, i64, i32, i32, i32, vp, vp]),
     "fus_fold_weight": (i32, [vp, vp, vp, i64, i32, i32, i64, vp, vp]),
     "fus_scale_sum_planes": (i32, [vp, i32, i64, i32, i32, vp, vp, i64, vp, vp]),
     "fus_ep_p2p_decode_forward": (i32, [vp, vp, vp, i32, vp, vp, vp, vp, vp, sz, vp, vp]),

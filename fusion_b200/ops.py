@@ -290,6 +290,18 @@ def scale_sum_planes(partial, nsplit: int, row_scale, out):
            _ld(out), _stream(), _sp())
 
 
+def fp8_block_dequant(src, scale, dst, block=(128, 128)):
+    """dst (bf16, rows x cols) = fp8 e4m3 src * scale per block (scale [ceil(R/br),
+    ceil(C/bc)] fp32)."""
+    if src.dtype != torch.float8_e4m3fn or dst.dtype != torch.bfloat16:
+        raise TypeError("fp8_block_dequant: e4m3 source and bf16 destination required")
+    cols = src.shape[-1]
+    rows = src.numel() // cols
+    sc = scale.reshape(-1, scale.shape[-1])
+    L.call("fus_fp8_block_dequant", _p(src), _p(sc), sc.stride(0), _p(dst), rows, cols,
+           block[0], block[1], _stream(), _sp())
+
+
 def add(a, b, o):
     M, N = a.shape
     L.call("fus_add", _p(a), _ld(a), _p(b), _ld(b), _p(o), _ld(o), M, N, _stream(), _sp())

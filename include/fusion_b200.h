@@ -313,6 +313,14 @@ int fus_scale_sum_planes(const float* partial, int nsplit, long plane, int T, in
                          const float* row_scale, float* out, long ldo, void* stream, int* status);
 
 /* ---------------------------------------------------------------------------------
+ * Checkpoint ingest: FP8 (e4m3) weights with one fp32 scale per br x bc block (the
+ * `weight_scale_inv` of block-quantised MoE checkpoints), dequantised to bf16 at load:
+ *   dst[r, c] = bf16(fp8(src[r, c]) * scale[(r / br) * scale_ld + c / bc])
+ * rows x cols row-major, cols % 8 == 0, bc % 8 == 0. */
+int fus_fp8_block_dequant(const void* src, const float* scale, long scale_ld, void* dst, long rows,
+                          int cols, int br, int bc, void* stream, int* status);
+
+/* ---------------------------------------------------------------------------------
  * Element-wise / merge kernels
  * ------------------------------------------------------------------------------- */
 /* glm52/kernels/moe_gateup.py:251 launch_silu_and_mul; reference.py:36-40:

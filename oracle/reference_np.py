@@ -275,3 +275,27 @@ def router_logits_exact_fp32(h: np.ndarray, w: np.ndarray, gate_w: np.ndarray,
     hf = h.astype(np.float32)
     xn = hf * row_rstd(h, eps)[:, None] * w.astype(np.float32)
     return (xn @ gate_w.astype(np.float32).T).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------------
+# FP8 checkpoint ingest  (no reference counterpart: FP8 is out of scope there,
+# glm52_h200/README.md:194; the format is the e4m3 + per-128x128-block scale of
+# block-quantised MoE checkpoints)
+# ---------------------------------------------------------------------------------
+def e4m3_to_f32(bits: np.ndarray) -> np.ndarray:
+    """OCP FP8 E4M3 (fn variant: no infinities, S.1111.111 = NaN) decoded from its bits."""
+    b = bits.astype(np.uint32)
+    sign = np.where(b >> 7, -1.0, 1.0)
+    exp = (b >> 3) & 0xF
+    man = (b & 7).astype(np.float64)
+    val = np.where(exp == 0, man / 8.0 * 2.0 ** -6, (1.0 + man / 8.0) * 2.0 ** (exp.astype(np.float64) - 7))
+    val = np.where((exp == 15) & ((b & 7) == 7), np.nan, val)
+    return (sign * val).astype(np.float32)
+
+
+def fp8_block_dequant(bits: np.ndarray, scale: np.ndarray, block=(128, 128)) -> np.ndarray:
+    """bf16(e4m3(bits) * scale[r // br, c // bc]) (fp32 product, one rounding)."""
+    br, bc = block
+    R, C = bits.shape
+    s = np.repeat(np.repeat(scale.astype(np.float32), br, 0), bc, 1)[:R, :C]
+    return bf16(e4m3_to_f32(bits) * s)

@@ -5,8 +5,9 @@ weights, routing frozen from the pipeline's own x2 with a zero correction bias, 
 reference output), `build_chain(p, cfg, sel, shared_cfg)` returning the list of launches
 for one fusion configuration, `CONFIGS`, and `main()` which checks every configuration
 against the fp32 reference (tol 5e-2, bench_layer.py:573) and times it as one chain with
-one L2 flush per repetition. The o_proj / ResAdd1 axis of the reference is outside the
-MoE block and is not reproduced: the chain starts at ResAdd+RMSNorm on (c, h_in).
+one L2 flush per repetition. The chain starts at o_proj (S3/S4, bench_layer.py:399-415):
+`resadd1="in_oproj"` is fusion #1 (h1 = a_attn @ w_o + h_in in one GEMM, then norm only),
+"separate" writes c = a_attn @ w_o and the norm axis adds h_in.
 
 Extra configuration `Z_block`: the whole block as one C-ABI call (fus_moe_block_forward),
 which computes its own routing.
@@ -29,6 +30,7 @@ from ..kernels import layout as KL
 from ..kernels import moe_down_merge as KD
 from ..kernels import moe_gateup as KG
 from ..kernels import norm_router as KR
+from ..kernels import oproj_resadd as KO
 
 H = C.HIDDEN_SIZE
 I = C.MOE_INTERMEDIATE_SIZE
@@ -59,7 +61,7 @@ def load_cfgs(regime: str) -> dict:
     T = REGIMES[regime]
     bm = 16 if T * TOPK / E <= 16 else 32 if T * TOPK / E <= 64 else 64 if T * TOPK / E <= 160 else 128
     g = {"BLOCK_M": bm}
-    return {"add": {}, "norm": {}, "addnorm": {}, "router": {}, "topk": {}, "w13": g,
+    return {"oproj": {}, "add": {}, "norm": {}, "addnorm": {}, "router": {}, "topk": {}, "w13": g,
             "w13_fused": g, "act": {}, "w2": g, "w2_fused8": g, "w2_fused9": g,
             "moe_sum": {}, "resadd2": {}}
 
@@ -72,9 +74,14 @@ class LayerProblem:
         d = synth.Dims()
         w = weights if weights is not None else synth.make_block_weights(seed, d, dev)
         self.weights = w
-        # the chain's inputs: attention-block output `c` and the residual `h_in`
-        self.c = synth.make("h", (T, H), seed * 7919 + T, dev)
+        # the chain's inputs: attention output `a_attn`, o_proj weight `w_o` [K, H] and the
+        # residual `h_in`; c = a_attn @ w_o is the o_proj output of the unfused chain
+        self.Kq = C.OPROJ_K_PREFILL if regime.startswith("prefill") else C.OPROJ_K_DECODE
+        self.a_attn = synth.make("a_attn", (T, self.Kq), seed * 7919 + T, dev)
+        self.w_o = synth.make("w_o", (self.Kq, H), seed + 17, dev)
         self.h_in = synth.make("r", (T, H), seed * 7919 + T, dev)
+        self.c = torch.empty(T, H, dtype=bf, device=dev)
+        self.acc32 = torch.zeros(T, H, dtype=torch.float32, device=dev)
         self.h1 = torch.empty(T, H, dtype=bf, device=dev)
         self.w_norm = w["gamma"]
         self.x2 = torch.empty(T, H, dtype=bf, device=dev)
@@ -96,6 +103,7 @@ class LayerProblem:
 
         # routing frozen from the pipeline's own x2 (bench_layer.py:348-363), zero bias
         with torch.no_grad():
+            KO.gemm_launch(self.a_attn, self.w_o, self.c, None, {}, False, False)
             KN.fused_add_rmsnorm(self.c, self.h_in, self.w_norm, self.h1, self.x2, {})
             KR.router_gemm(self.x2, self.wg_t, self.logits, {})
             KR.topk_only(self.logits, self.topw, self.topi, {})
@@ -137,13 +145,20 @@ class LayerProblem:
 def build_chain(p: LayerProblem, cfg: dict, sel: dict, shared_cfg: dict) -> list:
     fns = []
     L = cfg
+    # ---- o_proj (+ ResAdd1) ----
+    if sel.get("resadd1") == "in_oproj":  # fusion #1
+        fns += KO.make_fused_chain(p.a_attn, p.w_o, p.h_in, p.h1, p.acc32, L["oproj"])
+    else:
+        fns += [lambda: KO.gemm_launch(p.a_attn, p.w_o, p.c, None, L["oproj"], False, False)]
     if sel.get("block"):
         blk = shared_cfg["block"]
         outs = BlockOutputs(out=p.out, h1=p.h1, topw=p.topw_scratch, topi=p.topi_scratch)
-        return [lambda: blk.forward(p.c, p.h_in, outs)]
+        return fns + [lambda: blk.forward(p.c, p.h_in, outs)]
 
     # ---- ResAdd + RMSNorm ----
-    if sel["norm"] == "fused3":
+    if sel.get("resadd1") == "in_oproj":  # the residual is already in h1
+        fns += [lambda: KN.norm_only(p.h1, p.w_norm, p.x2, L["norm"])]
+    elif sel["norm"] == "fused3":
         fns += [lambda: KN.fused_add_rmsnorm(p.c, p.h_in, p.w_norm, p.h1, p.x2, L["addnorm"])]
     else:
         fns += [lambda: KN.add_only(p.c, p.h_in, p.h1, L["add"]),
@@ -212,17 +227,19 @@ def tune_shared(p: LayerProblem) -> dict:
 
 
 CONFIGS = {
-    "A_all_unfused": dict(norm="split", gateup="split", down="split"),
-    "B_f3": dict(norm="fused3", gateup="split", down="split"),
-    "D_f6": dict(norm="split", gateup="fused6", down="split"),
-    "E_f10": dict(norm="split", gateup="split", down="merge_f10"),
-    "F_f8": dict(norm="split", gateup="split", down="atomic8"),
-    "G_f9": dict(norm="split", gateup="split", down="atomic9"),
-    "H_f3_f10": dict(norm="fused3", gateup="split", down="merge_f10"),
-    "I_f3_f9": dict(norm="fused3", gateup="split", down="atomic9"),
-    "J_f3_f6_f10": dict(norm="fused3", gateup="fused6", down="merge_f10"),
-    "K_f3_f8": dict(norm="fused3", gateup="split", down="atomic8"),
-    "Z_block": dict(block=True),
+    "A_all_unfused": dict(resadd1="separate", norm="split", gateup="split", down="split"),
+    "B_f3": dict(resadd1="separate", norm="fused3", gateup="split", down="split"),
+    "C_f1": dict(resadd1="in_oproj", norm="split", gateup="split", down="split"),
+    "D_f6": dict(resadd1="separate", norm="split", gateup="fused6", down="split"),
+    "E_f10": dict(resadd1="separate", norm="split", gateup="split", down="merge_f10"),
+    "F_f8": dict(resadd1="separate", norm="split", gateup="split", down="atomic8"),
+    "G_f9": dict(resadd1="separate", norm="split", gateup="split", down="atomic9"),
+    "H_f3_f10": dict(resadd1="separate", norm="fused3", gateup="split", down="merge_f10"),
+    "I_f3_f9": dict(resadd1="separate", norm="fused3", gateup="split", down="atomic9"),
+    "J_f1_f6_f9": dict(resadd1="in_oproj", norm="split", gateup="fused6", down="atomic9"),
+    "K_f3_f8": dict(resadd1="separate", norm="fused3", gateup="split", down="atomic8"),
+    "L_f3_f6_f10": dict(resadd1="separate", norm="fused3", gateup="fused6", down="merge_f10"),
+    "Z_block": dict(resadd1="separate", block=True),
 }
 
 

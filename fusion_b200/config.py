@@ -20,6 +20,10 @@ TOPK_METHOD = "noaux_tc"
 N_GROUP = 1
 TOPK_GROUP = 1
 RMS_NORM_EPS = 1e-5
+# o_proj contraction width (glm52/config.py:55-59): absorbed MLA at decode emits
+# [T, heads, kv_lora_rank], non-absorbed MLA at prefill [T, heads, v_head_dim]
+OPROJ_K_DECODE = 64 * 512  # 32768
+OPROJ_K_PREFILL = 64 * 256  # 16384
 W13_N = 2 * MOE_INTERMEDIATE_SIZE
 W2_K = MOE_INTERMEDIATE_SIZE
 

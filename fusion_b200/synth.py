@@ -29,6 +29,8 @@ STREAMS: dict[str, tuple[int, float, float, torch.dtype]] = {
     "w2": (7, 0.0, 0.02, torch.bfloat16),
     "w13s": (8, 0.0, 0.02, torch.bfloat16),
     "w2s": (9, 0.0, 0.02, torch.bfloat16),
+    "a_attn": (10, 0.0, 0.05, torch.bfloat16),  # attention output entering o_proj
+    "w_o": (11, 0.0, 0.02, torch.bfloat16),     # o_proj weight [K, H]
 }
 
 

@@ -268,7 +268,7 @@ __global__ void permute_rows_kernel(const __nv_bfloat16* __restrict__ src, long 
     if (id >= num_valid) continue;  // dispatch pad: never multiplied, left as is
     uint4* d = reinterpret_cast<uint4*>(dst + (long)p * ld_dst);
     const uint4* s = reinterpret_cast<const uint4*>(src + (long)(id / div) * ld_src);
-    for (int v = threadIdx.x & 31; v < nv; v += 32) d[v] = __ldg(s + v);
+    warp_copy_row(d, s, nv, threadIdx.x & 31);
   }
 }
 

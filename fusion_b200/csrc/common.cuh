@@ -204,6 +204,21 @@ FUS_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.re
 // all committed stores are complete in global memory
 FUS_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// One warp copies a row of nv 16-byte vectors, eight loads in flight per lane (a plain
+// strided loop keeps one load per lane outstanding and is latency-bound on 12 KB rows)
+FUS_DEVICE void warp_copy_row(uint4* __restrict__ d, const uint4* __restrict__ s, int nv,
+                              int lane) {
+  int v = lane;
+  for (; v + 7 * 32 < nv; v += 8 * 32) {
+    uint4 t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t[u] = __ldg(s + v + u * 32);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) d[v + u * 32] = t[u];
+  }
+  for (; v < nv; v += 32) d[v] = __ldg(s + v);
+}
+
 // 16-byte global store with an L2 eviction-policy hint
 FUS_DEVICE void st_global_v4_hint(void* p, uint4 v, uint64_t policy) {
   asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x),

@@ -50,7 +50,7 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ x, long ldx, in
     const int id = __ldg(send_ids + p);
     const uint4* s = reinterpret_cast<const uint4*>(x + (long)(id / div) * ldx);
     uint4* d = reinterpret_cast<uint4*>(rows + (long)p * ldr);
-    for (int v = lane; v < (H >> 3); v += 32) d[v] = __ldg(s + v);
+    warp_copy_row(d, s, H >> 3, lane);
     if (lane == 0 && leid) leid_out[p] = __ldg(leid + id);
   }
 }
@@ -64,7 +64,7 @@ __global__ void ep_unpack_kernel(const __nv_bfloat16* __restrict__ rows, long ld
     const int id = __ldg(send_ids + p);
     const uint4* s = reinterpret_cast<const uint4*>(rows + (long)p * ldr);
     uint4* d = reinterpret_cast<uint4*>(y + (long)id * ldy);
-    for (int v = lane; v < (H >> 3); v += 32) d[v] = __ldg(s + v);
+    warp_copy_row(d, s, H >> 3, lane);
   }
 }
 
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(1024)
     if (slot < 0) continue;
     const uint4* s = reinterpret_cast<const uint4*>(x + (long)(i / topk) * ldx);
     uint4* d = reinterpret_cast<uint4*>(rows + (long)slot * ldr);
-    for (int v = lane; v < (H >> 3); v += 32) d[v] = __ldg(s + v);
+    warp_copy_row(d, s, H >> 3, lane);
   }
 }
 

@@ -273,12 +273,38 @@ extern "C" int fus_router_nsplit(int T, int H, int E, int nplanes) {
   const int bn = router_block_n(T);
   const long units = (long)(E / 128) * ceil_div(T, bn);
   const int ksteps = nplanes * H / 64;
-  long want = (num_sms() + units - 1) / units;
-  if (want > ksteps / 4) want = ksteps / 4;
-  if (want > 64) want = 64;
-  if (want < 1) want = 1;
-  const int kps = ceil_div(ksteps, want);
-  return ceil_div(ksteps, kps);  // the split count the GEMM will actually use
+  if (T < 1024) {
+    // weight-streaming regime: as many CTAs as the SMs take, each on its own K range
+    long want = (num_sms() + units - 1) / units;
+    if (want > ksteps / 4) want = ksteps / 4;
+    if (want > 64) want = 64;
+    if (want < 1) want = 1;
+    const int kps = ceil_div(ksteps, want);
+    return ceil_div(ksteps, kps);  // the split count the GEMM will actually use
+  }
+  // compute regime: K splits s minimising  waves(s) * (tile time / s)  +  partial-plane
+  // traffic(s):
+  // a tile's full-K time at the tensor peak per SM, waves over the CTA slots of this
+  // tile width, and s fp32 planes written and read back by the top-k
+  const double slots = (double)num_sms() * (bn <= 32 ? 3 : bn <= 64 ? 2 : 1);
+  const double tile_s = 2.0 * bn * 128 * (double)ksteps * 64 / 10.8e12;
+  const double plane_s = 2.0 * (double)T * E * 4 / 6.5e12;
+  int smax = ksteps / 4;
+  if (smax > 64) smax = 64;
+  if (smax < 1) smax = 1;
+  int best = 1;
+  double best_cost = 1e30;
+  for (int sp = 1; sp <= smax; ++sp) {
+    const int kps = ceil_div(ksteps, sp);
+    const int s = ceil_div(ksteps, kps);  // the split count the GEMM will actually use
+    const double waves = ceil((double)units * s / slots);
+    const double cost = waves * tile_s / s + s * plane_s;
+    if (cost < best_cost * (1 - 1e-9)) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 extern "C" int fus_router_logits(const void* x2, long ldx, const void* wa, int nplanes,

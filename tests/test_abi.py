@@ -82,3 +82,17 @@ def test_synth_host_deterministic_and_sliceable():
     assert abs(g.mean() - 1.0) < 2e-3 and abs(g.std() - 0.02) < 2e-3
     f = synth.make("gate_w", (4096,), 9).numpy()
     assert f.dtype == np.float32 and abs(f.std() - 0.02) < 2e-3
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    """No fallback: without the built library every entry point raises."""
+    import pytest
+
+    from fusion_b200 import _lib as L
+
+    monkeypatch.setattr(L, "_lib", None)
+    monkeypatch.setattr(L, "LIB_PATH", tmp_path / "libfusion_b200.so")
+    with pytest.raises(RuntimeError, match="not built"):
+        L.lib()
+    with pytest.raises(RuntimeError, match="not built"):
+        L.call("fus_version")

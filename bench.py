@@ -254,8 +254,8 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
         res = ({"topi": g.topi} if isinstance(g, EPDecodeStep) else g.res) if small else ep(h, r)
         torch.cuda.synchronize()
         ops.check_status()
-        if small and g.x is not None:
-            g.x.close()
+        if small:
+            g.close()  # collective: drops the graph, unmaps the peers' buffers
         barrier()
         ms_step = max_over_ranks(statistics.fmean(ms))
         # distinct experts over the whole job: union of every rank's routed ids
@@ -302,8 +302,7 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
         evs.append(a.elapsed_time(b))
     torch.cuda.synchronize()
     ops.check_status()
-    if ge.x is not None:
-        ge.x.close()
+    ge.close()
     barrier()
     e2e_ms = max_over_ranks(statistics.fmean(evs))
     if rank == 0:

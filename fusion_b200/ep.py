@@ -256,6 +256,10 @@ class EPDecodeStep:
         return self.out
 
     def close(self):
+        """Collective: drop the recorded step (it holds the peers' buffer addresses), then
+        unmap the peers' exchange buffers."""
+        torch.cuda.synchronize()
+        self.graph = None
         self.x.close()
 
 
@@ -289,6 +293,13 @@ class EPDecodeGraph:
     def replay(self):
         self.graph.replay()
         return self.out
+
+    def close(self):
+        """Collective when the exchange is NVLink: drop the graph, unmap the peers."""
+        torch.cuda.synchronize()
+        self.graph = None
+        if self.x is not None:
+            self.x.close()
 
 
 class CudaEPBackend:

@@ -113,8 +113,7 @@ def test_ep_single_rank_matches_block(T, fixed):
                 out = g.replay()
                 finish()
                 assert torch.equal(out.view(torch.int16), res["out"].view(torch.int16))
-            if g.x is not None:
-                g.x.close()
+            g.close()
         # the whole step as one library call (PDL-chained launches), eager and graphed
         st = EPDecodeStep(be, T)
         st.h.copy_(h)
@@ -183,7 +182,7 @@ def _two_rank_worker(rank, port, q):
         q.put((rank, (out.float().cpu().numpy(), out2.float().cpu().numpy(), same)))
         del g  # the graph holds NCCL work: release it before the communicator
         torch.cuda.synchronize()
-        gp.x.close()
+        gp.close()
         st.close()
         dist.barrier()
     finally:

@@ -85,6 +85,8 @@ class MoEBlock:
         assert h.is_contiguous() and r.is_contiguous() and h.shape == (T, self.H)
         if outs is None:
             outs = self.alloc_outputs(T)
+        if T == 0:  # an empty batch: nothing to compute
+            return outs
         nbytes = self.workspace_bytes(T, block_n)
         ws = workspace if workspace is not None else self._workspace(nbytes)
         L.call("fus_moe_block_forward", ctypes.byref(self.desc), h.data_ptr(), r.data_ptr(), T,

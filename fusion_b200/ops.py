@@ -21,8 +21,23 @@ ERR_TIMEOUT, ERR_BAD_EXPERT, ERR_CAPACITY = 0x1, 0x2, 0x4
 _status: dict[int, torch.Tensor] = {}
 
 
+_empty_anchor: dict[int, torch.Tensor] = {}
+
+
 def _p(t: torch.Tensor | None) -> int | None:
-    return None if t is None else t.data_ptr()
+    """Device address of `t`. An empty tensor has no storage (address 0); it is passed as
+    an aligned dummy address of its device so that a call over zero rows reaches the
+    library's empty-size early return instead of its null-pointer check."""
+    if t is None:
+        return None
+    if t.numel() == 0 and t.is_cuda:
+        idx = t.device.index if t.device.index is not None else torch.cuda.current_device()
+        a = _empty_anchor.get(idx)
+        if a is None:
+            a = torch.zeros(256, dtype=torch.uint8, device=t.device)
+            _empty_anchor[idx] = a
+        return a.data_ptr()
+    return t.data_ptr()
 
 
 def _stream() -> int:

@@ -222,3 +222,35 @@ def test_workspace_reused_across_sizes(weights_404):
         fresh = make_block(weights_404)(h, r)
         finish()
         assert torch.equal(o.out.view(torch.int16), fresh.out.view(torch.int16))
+
+
+def test_empty_batch_is_a_no_op(weights_404):
+    """T = 0 through the block and the drop-in entry points: no error, nothing written
+    (the reference's torch functions accept empty batches)."""
+    from fusion_b200 import ops
+    from fusion_b200.kernels import add_rmsnorm as KN
+    from fusion_b200.kernels import merge_resadd as KM
+    from fusion_b200.kernels import norm_router as KR
+
+    blk = make_block(weights_404)
+    h = torch.empty(0, D.H, dtype=torch.bfloat16, device=DEV)
+    o = blk(h, torch.empty_like(h))
+    assert o.out.shape == (0, D.H) and o.topi.shape == (0, D.topk)
+    KN.fused_add_rmsnorm(h, h, weights_404["gamma"], torch.empty_like(h), torch.empty_like(h), {})
+    lg = torch.empty(0, D.E, dtype=torch.float32, device=DEV)
+    KR.router_gemm(h, KR.wgt_from_gate(weights_404["gate_w"].to(torch.bfloat16)), lg, {})
+    KR.topk_only(lg, torch.empty(0, D.topk, device=DEV),
+                 torch.empty(0, D.topk, dtype=torch.int32, device=DEV), {})
+    y = torch.empty(0, D.topk, D.H, dtype=torch.bfloat16, device=DEV)
+    KM.fused_merge_resadd(y, torch.empty(0, D.topk, device=DEV), h, torch.empty_like(h), {})
+    ids = torch.empty(0, D.topk, dtype=torch.int32, device=DEV)
+    cap = D.E * 15 + 16
+    s = torch.full((cap,), -7, dtype=torch.int32, device=DEV)
+    e = torch.full((cap // 16,), -7, dtype=torch.int32, device=DEV)
+    n = torch.full((1,), -7, dtype=torch.int32, device=DEV)
+    ops.moe_align(ids, D.E, 16, s, e, n)
+    a = torch.empty(0, 32768, dtype=torch.bfloat16, device=DEV)
+    ops.oproj_resadd(a, torch.zeros(D.H, 32768, dtype=torch.bfloat16, device=DEV), h,
+                     torch.empty_like(h))
+    finish()
+    assert int(n.item()) == 0

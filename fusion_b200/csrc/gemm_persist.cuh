@@ -2,13 +2,15 @@
 // FUS_EPI_BF16 / FUS_EPI_SWIGLU, no split-K, no fused merge). Included by gemm.cu.
 //
 // One CTA per SM walks the same unit list as the one-tile-per-CTA kernel (stride
-// gridDim.x). The producer's ring runs continuously across units, so the next unit's
-// weight and token tiles stream in while the epilogue drains the current accumulators;
-// with block_n <= 128 the accumulators are double-buffered in TMEM, so the MMAs of the
-// next unit run while the epilogue drains the current one (with 256 the next unit's MMAs
-// wait for the drain). The epilogue
-// goes TMEM -> registers -> a 16 KB staging buffer per epilogue group -> 16-byte
-// stores, 64 tokens (32 for fp32 output) at a time.
+// gridDim.x). Warp 0 is the TMA producer (weight tiles; token tiles as one box sized to
+// the unit's live rows, or gathered four rows per gather4 by all 32 lanes), warp 1
+// issues the MMAs, and two groups of four warps drain the accumulators. The producer's
+// ring runs continuously across units, so the next unit's tiles stream in while the
+// epilogue drains; with block_n <= 128 the two accumulator sets are double-buffered in
+// TMEM and the next unit's MMAs run during the drain too (at 256 they fill TMEM and wait).
+// Epilogue: TMEM -> registers (SwiGLU / row scale / residual in fp32) -> a 16 KB staging
+// buffer per group -> TMA tile stores from alternating 8 KB halves for dense outputs, or
+// 16-byte stores through the row map for scattered ones.
 #pragma once
 
 // warp 0 TMA, warp 1 MMA, then two epilogue groups of four warps

@@ -83,6 +83,8 @@ class BlockDesc(C.Structure):
         ("w2", vp),
         ("w13s", vp),
         ("w2s", vp),
+        ("n_group", i32),
+        ("topk_group", i32),
     ]
 
 

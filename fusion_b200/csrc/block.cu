@@ -151,10 +151,10 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   if (small) {
     // decode: norm + router + top-k + layout in one launch; it also clears the merge
     // counters, so the down projection needs no separate reset
-    if ((rc = fus_moe_route_small(h, r, d->gamma, d->eps, d->wa, d->nplanes, d->bias, T, H, E, K,
-                                  d->routed_scale, d->renorm, h1, x2, partial, topw, topi,
-                                  block_n, sorted, L.cap, eids, L.blocks_cap, ntp, done, counters,
-                                  T * L.tiles, stream, status)))
+    if ((rc = route_small_launch(h, r, d->gamma, d->eps, d->wa, d->nplanes, d->bias, T, H, E, K,
+                                 d->routed_scale, d->renorm, d->n_group, d->topk_group, h1, x2,
+                                 partial, topw, topi, block_n, sorted, L.cap, eids, L.blocks_cap,
+                                 ntp, done, counters, T * L.tiles, stream, status)))
       return rc;
   } else {
     if ((rc = fus_add_rmsnorm(h, H, r, H, d->gamma, h1, H, x2, H, T, H, d->eps, 1, 1, stream,
@@ -163,8 +163,10 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
     if ((rc = fus_router_logits(x2, H, d->wa, d->nplanes, partial, T, H, E, L.nsplit, stream,
                                 status)))
       return rc;
-    if ((rc = fus_router_topk(partial, L.nsplit, d->bias, nullptr, topw, topi, T, E, K,
-                              d->routed_scale, d->renorm, stream, status)))
+    if ((rc = fus_router_topk_grouped(partial, L.nsplit, d->bias, nullptr, topw, topi, T, E, K,
+                                      d->n_group > 1 ? d->n_group : 1,
+                                      d->topk_group > 1 ? d->topk_group : 1, d->routed_scale,
+                                      d->renorm, stream, status)))
       return rc;
     // balanced layout: an expert just over a block fills two even blocks, not a full
     // block plus a few stragglers that stream the same weights again

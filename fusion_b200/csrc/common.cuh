@@ -219,6 +219,46 @@ FUS_DEVICE void warp_copy_row(uint4* __restrict__ d, const uint4* __restrict__ s
   for (; v < nv; v += 32) d[v] = __ldg(s + v);
 }
 
+// noaux_tc group masking for one token held by a warp, lane l owning choice values of
+// experts 8l .. 8l+7 (reference.py:159-166): a group of E/n_group consecutive experts
+// spans (E/n_group)/8 lanes; its score is the sum of its two largest choice values;
+// experts outside the topk_group best groups (ties: lower group index) get choice * 0.
+// n_group == 1 leaves ch untouched. Groups of 8 * 2^j experts, n_group <= 32.
+FUS_DEVICE void group_mask_choice(float* ch, int lane, int E, int n_group, int topk_group) {
+  if (n_group <= 1) return;
+  float a1 = -INFINITY, a2 = -INFINITY;  // this lane's two largest
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float v = ch[j];
+    if (v > a1) {
+      a2 = a1;
+      a1 = v;
+    } else if (v > a2) {
+      a2 = v;
+    }
+  }
+  const int lpg = (E / n_group) >> 3;  // lanes per group
+  for (int o = 1; o < lpg; o <<= 1) {  // merge the top-2 of lane pairs within a group
+    const float b1 = __shfl_xor_sync(0xffffffffu, a1, o);
+    const float b2 = __shfl_xor_sync(0xffffffffu, a2, o);
+    const float hi = fmaxf(a1, b1);
+    const float lo = fmaxf(fminf(a1, b1), fmaxf(a2, b2));
+    a1 = hi;
+    a2 = lo;
+  }
+  const float gscore = a1 + a2;  // the reference sums its descending top-2 values
+  const int my_g = lane / lpg;
+  int better = 0;  // groups ranked ahead of mine
+  for (int g = 0; g < n_group; ++g) {
+    const float og = __shfl_sync(0xffffffffu, gscore, g * lpg);
+    better += (og > gscore) || (og == gscore && g < my_g);
+  }
+  if (lane * 8 < E && better >= topk_group) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ch[j] = ch[j] * 0.0f;
+  }
+}
+
 // 16-byte global store with an L2 eviction-policy hint
 FUS_DEVICE void st_global_v4_hint(void* p, uint4 v, uint64_t policy) {
   asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x),

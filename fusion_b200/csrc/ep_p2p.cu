@@ -308,8 +308,8 @@ extern "C" int fus_ep_p2p_decode_forward(const fus_ep_p2p_desc* d, const void* h
   const bool shared = b->w13s != nullptr;
   int rc;
   // 1 norm + router + top-k (its layout over all experts goes to scratch)
-  if ((rc = fus_moe_route_small(h, r, b->gamma, b->eps, b->wa, b->nplanes, b->bias, T, H, E, K,
-                                b->routed_scale, b->renorm, h1, x2,
+  if ((rc = route_small_launch(h, r, b->gamma, b->eps, b->wa, b->nplanes, b->bias, T, H, E, K,
+                                b->routed_scale, b->renorm, b->n_group, b->topk_group, h1, x2,
                                 reinterpret_cast<float*>(at(L.off_logits)), topw, topi, 16,
                                 reinterpret_cast<int*>(at(L.off_rs)), L.rs_cap,
                                 reinterpret_cast<int*>(at(L.off_reids)), L.rs_bcap,

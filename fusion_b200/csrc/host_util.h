@@ -51,6 +51,14 @@ int oproj_finish(const float* part, long plane, int S, long ldp, const void* res
                  void* out, long ldo, int T, int N, int round_mid, void* stream,
                  int out_f32 = 0, int accumulate = 0, const float* row_scale = nullptr);
 
+// the fused decode front end with noaux_tc group masking (fus_moe_route_small is n_group 1)
+int route_small_launch(const void* h, const void* r, const void* gamma, float eps, const void* wa,
+                       int nplanes, const float* bias, int T, int H, int E, int topk, float scale,
+                       int renorm, int n_group, int topk_group, void* h1, void* x2, float* logits,
+                       float* topw, int* topi, int block_m, int* sorted_ids, int sorted_cap,
+                       int* expert_ids, int blocks_cap, int* ntp, int* done, int* zero,
+                       int zero_n, void* stream, int* status);
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }

@@ -31,6 +31,7 @@ struct RouteArgs {
   int T, H, E, topk;
   float scale;
   int renorm;
+  int n_group, topk_group;
   __nv_bfloat16* h1;
   __nv_bfloat16* x2;
   float* logits;
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(kRouteThreads)
         ix[j] = 0x7fffffff;
       }
     }
+    group_mask_choice(ch, lane, E, a.n_group, a.topk_group);
     // sort the lane's 8 descending by (ch, then lower expert id): odd-even transposition
 #pragma unroll
     for (int pass = 0; pass < 8; ++pass)
@@ -322,13 +324,20 @@ __global__ void __launch_bounds__(kRouteThreads)
 
 using namespace fus;
 
-extern "C" int fus_moe_route_small(const void* h, const void* r, const void* gamma, float eps,
-                                   const void* wa, int nplanes, const float* bias, int T, int H,
-                                   int E, int topk, float scale, int renorm, void* h1, void* x2,
-                                   float* logits, float* topw, int* topi, int block_m,
-                                   int* sorted_ids, int sorted_cap, int* expert_ids,
-                                   int blocks_cap, int* ntp, int* done, int* zero, int zero_n,
-                                   void* stream, int* status) {
+namespace fus {
+int route_small_launch(const void* h, const void* r, const void* gamma, float eps, const void* wa,
+                       int nplanes, const float* bias, int T, int H, int E, int topk, float scale,
+                       int renorm, int n_group, int topk_group, void* h1, void* x2, float* logits,
+                       float* topw, int* topi, int block_m, int* sorted_ids, int sorted_cap,
+                       int* expert_ids, int blocks_cap, int* ntp, int* done, int* zero,
+                       int zero_n, void* stream, int* status) {
+  if (n_group < 1) n_group = 1;
+  if (topk_group < 1) topk_group = 1;
+  if (n_group > 1 && (E % n_group || (E / n_group) % 8 ||
+                      ((E / n_group / 8) & (E / n_group / 8 - 1)) || n_group > 32 ||
+                      topk_group > n_group || topk > topk_group * (E / n_group)))
+    return set_error(FUS_E_UNSUPPORTED, "route_small: n_group=%d topk_group=%d E=%d", n_group,
+                     topk_group, E);
   if (!h || !r || !gamma || !wa || !h1 || !x2 || !logits || !topw || !topi || !sorted_ids ||
       !expert_ids || !ntp || !done || (zero_n > 0 && !zero))
     return set_error(FUS_E_INVALID, "route_small: null argument");
@@ -365,6 +374,8 @@ extern "C" int fus_moe_route_small(const void* h, const void* r, const void* gam
   a.topk = topk;
   a.scale = scale;
   a.renorm = renorm;
+  a.n_group = n_group;
+  a.topk_group = topk_group;
   a.h1 = (__nv_bfloat16*)h1;
   a.x2 = (__nv_bfloat16*)x2;
   a.logits = logits;
@@ -382,4 +393,17 @@ extern "C" int fus_moe_route_small(const void* h, const void* r, const void* gam
   a.status = status;
   route_small_kernel<<<E / kRouteExperts, kRouteThreads, dyn, as_stream(stream)>>>(a);
   return check_launch("route_small");
+}
+}  // namespace fus
+
+extern "C" int fus_moe_route_small(const void* h, const void* r, const void* gamma, float eps,
+                                   const void* wa, int nplanes, const float* bias, int T, int H,
+                                   int E, int topk, float scale, int renorm, void* h1, void* x2,
+                                   float* logits, float* topw, int* topi, int block_m,
+                                   int* sorted_ids, int sorted_cap, int* expert_ids,
+                                   int blocks_cap, int* ntp, int* done, int* zero, int zero_n,
+                                   void* stream, int* status) {
+  return route_small_launch(h, r, gamma, eps, wa, nplanes, bias, T, H, E, topk, scale, renorm, 1,
+                            1, h1, x2, logits, topw, topi, block_m, sorted_ids, sorted_cap,
+                            expert_ids, blocks_cap, ntp, done, zero, zero_n, stream, status);
 }

@@ -91,43 +91,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32)
       ch[j] = -INFINITY;
     }
   }
-  if (n_group > 1) {
-    // noaux_tc group masking (reference.py:159-166): group score = sum of the group's two
-    // largest choice values; experts outside the topk_group best groups get choice * 0
-    // (0 or -0, as the reference's multiply by the 0/1 mask). A group of gs = E/n_group
-    // consecutive experts spans gs/8 consecutive lanes (gs % 8 == 0, host check).
-    float a1 = -INFINITY, a2 = -INFINITY;  // this lane's two largest
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float v = ch[j];
-      if (v > a1) {
-        a2 = a1;
-        a1 = v;
-      } else if (v > a2) {
-        a2 = v;
-      }
-    }
-    const int lpg = (E / n_group) >> 3;  // lanes per group (a power of two here)
-    for (int o = 1; o < lpg; o <<= 1) {  // merge the top-2 of lane pairs within a group
-      const float b1 = __shfl_xor_sync(0xffffffffu, a1, o);
-      const float b2 = __shfl_xor_sync(0xffffffffu, a2, o);
-      const float hi = fmaxf(a1, b1);
-      const float lo = fmaxf(fminf(a1, b1), fmaxf(a2, b2));
-      a1 = hi;
-      a2 = lo;
-    }
-    const float gscore = a1 + a2;  // the reference sums its descending top-2 values
-    const int my_g = lane / lpg;
-    int better = 0;  // groups ranked ahead of mine (score, then lower group index)
-    for (int g = 0; g < n_group; ++g) {
-      const float og = __shfl_sync(0xffffffffu, gscore, g * lpg);
-      better += (og > gscore) || (og == gscore && g < my_g);
-    }
-    if (e0 < E && better >= topk_group) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ch[j] = ch[j] * 0.0f;
-    }
-  }
+  group_mask_choice(ch, lane, E, n_group, topk_group);
   unsigned used = 0;
   float my_w = 0.f;
   int my_id = 0;

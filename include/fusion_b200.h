@@ -378,6 +378,8 @@ typedef struct fus_moe_block_desc {
   const void* w2;     /* [E, H, I] bf16                           */
   const void* w13s;   /* shared expert [2I, H] bf16 or NULL       */
   const void* w2s;    /* shared expert [H, I] bf16 or NULL        */
+  int n_group;        /* noaux_tc groups (0 or 1: none; GLM-5.2)  */
+  int topk_group;     /* groups kept when n_group > 1             */
 } fus_moe_block_desc;
 
 int fus_moe_block_pick_block_n(int T, int E, int topk);

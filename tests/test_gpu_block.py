@@ -254,3 +254,33 @@ def test_empty_batch_is_a_no_op(weights_404):
                      torch.empty_like(h))
     finish()
     assert int(n.item()) == 0
+
+
+@pytest.mark.parametrize("T", [1, 9, 64])
+def test_grouped_routing_block(weights_404, T):
+    """noaux_tc group masking (n_group 8, topk_group 4) through the whole block: the fused
+    decode front end (T <= 16) and the separate router kernels give the oracle's grouped
+    ids wherever the choice scores are separated, and the block output stays within the
+    exact-fp32 bar computed from those ids."""
+    w = weights_404
+    blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"],
+                   n_group=8, topk_group=4)
+    h, r = synth.make_inputs(123 + T, T, D, DEV)
+    o = blk(h, r)
+    finish()
+    x2, h1 = O.add_rmsnorm(to_np(h), to_np(r), to_np(w["gamma"]))
+    lg = O.router_logits(x2, w["gate_w"].cpu().numpy())
+    ow, oi = O.router_select(lg, w["bias"].cpu().numpy(), n_group=8, topk_group=4)
+    ti = o.topi.cpu().numpy()
+    # the masked choice scores: rows whose top-9 are separated by > 1e-5 must match exactly
+    ch = O.sigmoid(lg) + w["bias"].cpu().numpy()
+    g = ch.reshape(T, 8, D.E // 8)
+    keep = O.topk_desc(np.sort(g, -1)[..., -2:].sum(-1), 4)
+    mask = np.zeros((T, 8), dtype=np.float32)
+    np.put_along_axis(mask, keep, 1.0, axis=1)
+    ch = (g * mask[..., None]).reshape(T, D.E)
+    top9 = -np.sort(-ch, axis=1)[:, :9]
+    clear = np.all(np.diff(-top9, axis=1) > 1e-5, axis=1)
+    assert np.array_equal(ti[clear], oi[clear])
+    same = np.all(ti == oi, axis=1)
+    np.testing.assert_allclose(o.topw.cpu().numpy()[same], ow[same], rtol=2e-5, atol=2e-6)

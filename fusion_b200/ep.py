@@ -20,7 +20,7 @@ exchange over gloo with a numpy backend. Small batches (decode) exchange fixed s
 blocks: over NCCL all_to_all (`forward_fixed`), or with `P2PExchange` by direct stores
 into the peers' exchange buffers over NVLink and flag waits (`forward_p2p`, no
 collective launch at all). The reference has no multi-GPU path
-(log/LOG-00-plan-and-filter.md:41); SURVEY §8e gives the design.
+(log/LOG-00-plan-and-filter.md:41).
 """
 
 from __future__ import annotations

@@ -3,11 +3,11 @@
 Runs the REFERENCE's own torch functions (glm52_h200/reference.py, imported from a
 checkout of HansonZhang-cuhksz/fusion) on seeded inputs from fusion_b200's
 bit-reproducible generator and stores inputs (when small) and outputs as .npz.
-Needs the reference checkout (``FUSION_REFERENCE`` or /root/reference) and the
+Needs a checkout of the reference (its directory in ``FUSION_REFERENCE``) and the
 built library (for the host-side generator); the committed .npz files are what the
 tests read, so the reference is not needed at test time.
 
-    python tests/golden/make_golden.py
+    FUSION_REFERENCE=<checkout of HansonZhang-cuhksz/fusion> python tests/golden/make_golden.py
 """
 
 from __future__ import annotations
@@ -22,7 +22,9 @@ import torch
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, os.environ.get("FUSION_REFERENCE", "/root/reference"))
+if "FUSION_REFERENCE" not in os.environ:
+    raise SystemExit("set FUSION_REFERENCE to a checkout of HansonZhang-cuhksz/fusion")
+sys.path.insert(0, os.environ["FUSION_REFERENCE"])
 
 import glm52_h200.reference as R  # noqa: E402  (the reference under test)
 

@@ -3,6 +3,7 @@
     python -m fusion_b200.bench.profile_case decode  [reps]
     python -m fusion_b200.bench.profile_case prefill [reps]
     python -m fusion_b200.bench.profile_case prefill32 [reps]
+    python -m fusion_b200.bench.profile_case block8192 [reps]   (any block<T>)
 
 decode : the w13+SwiGLU and w2 launches of the decode block at T=1 — 8 routed experts
          with one token each plus the shared expert (the same tile shapes, flags and
@@ -11,6 +12,7 @@ prefill: 16 experts x 256 tokens each (the per-expert load of T=8192 over 256 ex
          256-token tiles with two weight tiles per CTA.
 prefill32: the same on 32 experts (2.4 GB of weights; several tiles per SM, so the
          persistent kernel's steady state dominates rather than its tail).
+block<T>: the whole MoE block (MoEBlock.forward, seeded GLM-5.2 weights) on T tokens.
 Each launch is timed with CUDA events; the line printed gives us and TB/s or TF/s.
 """
 
@@ -23,7 +25,30 @@ import torch
 from .. import ops, synth
 
 
+def block_case(T: int, reps: int) -> None:
+    from ..block import MoEBlock
+
+    d = synth.Dims()
+    w = synth.make_block_weights(1, d, "cuda")
+    blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"])
+    h, r = synth.make_inputs(1000 + T, T, d, "cuda")
+    blk(h, r)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    ev[0].record()
+    for i in range(reps):
+        blk(h, r)
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    ops.check_status()
+    ts = [ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(reps)]
+    print(f"block T={T}: " + " ".join(f"{t:.0f}" for t in ts) + " us per call")
+
+
 def main(case: str, reps: int = 3) -> None:
+    if case.startswith("block"):
+        block_case(int(case[5:]), reps)
+        return
     H, I, K = 6144, 2048, 8
     E = 32 if case == "prefill32" else 16
     w13 = synth.make("w13", (E, 2 * I, H), 1, "cuda")

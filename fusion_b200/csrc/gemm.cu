@@ -498,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 #include "gemm_persist.cuh"
+#include "gemm_pair.cuh"
 
 // ======================================================================================
 // host side
@@ -529,6 +530,37 @@ int launch_persist(int bn, const CUtensorMap* maps, const GemmArgs& a, int grid,
     case 256: return launch_p<256, EPI>(maps, a, grid, st);
   }
   return set_error(FUS_E_UNSUPPORTED, "persistent GEMM: block_n %d", bn);
+}
+
+template <int EPI>
+int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStream_t st) {
+  using Cfg = PairCfg<EPI>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  static int max_clusters = 0;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(grouped_gemm_pair<EPI>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (attr_err != cudaSuccess) return;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    if (cudaOccupancyMaxActiveClusters(&max_clusters, grouped_gemm_pair<EPI>, &cfg) !=
+        cudaSuccess) {
+      (void)cudaGetLastError();
+      max_clusters = 0;
+    }
+  });
+  if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
+                                                cudaGetErrorString(attr_err));
+  // one resident cluster per SM pair; clusters beyond the co-resident count would only
+  // queue behind the first wave
+  long clusters = max_clusters > 0 ? max_clusters : num_sms() / 2;
+  if (clusters > total) clusters = total;
+  grouped_gemm_pair<EPI><<<(int)(2 * clusters), kPThreads, Cfg::SMEM_BYTES, st>>>(
+      maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[4], maps[5], a);
+  return check_launch("grouped_gemm_pair");
 }
 
 template <int BN, int EPI, int MT>
@@ -764,6 +796,47 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
   if (mt2 && epilogue != FUS_EPI_F32 && !merge && pdl == 0 && a.ksplit == 1 &&
       total > 2L * sms &&
       !(groups[0].flags & FUS_GEMM_NO_PERSIST)) {
+    // SM pairs (2-CTA clusters, M = 256 tiles) for 256-token blocks with dense outputs
+    bool pair = block_n == kPairBN && a_kplanes == 1 && !(groups[0].flags & FUS_GEMM_NO_PAIR) &&
+                (epilogue == FUS_EPI_BF16 || w_rows % 512 == 0);
+    for (int g = 0; g < ngroups && pair; ++g) {
+      const fus_gemm_group& G = groups[g];
+      pair = !G.gather_ids && !G.row_map && !G.row_scale && !G.res && G.row_limit >= 1;
+    }
+    if (pair) {
+      a.m_tiles = epilogue == FUS_EPI_SWIGLU ? w_rows / 512 : w_rows / 256;
+      long pu[2] = {0, 0};
+      for (int g = 0; g < ngroups; ++g) {
+        const fus_gemm_group& G = groups[g];
+        pu[g] = (long)G.max_blocks * a.m_tiles;
+        const bool out32 = epilogue == FUS_EPI_BF16 && (G.flags & FUS_GEMM_OUT_F32);
+        int rc = make_tmap_store_2d(&maps[4 + g], G.out, out32, (uint64_t)out_cols,
+                                    (uint64_t)G.row_limit, (uint64_t)G.ldo, 128, out32 ? 16 : 32);
+        // token maps: boxes of 128 / 16 / 64 rows (one CTA's half of a block)
+        if (!rc)
+          rc = make_tmap_bf16_2d(&maps[2 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
+                                 (uint64_t)G.ldx, kBK, kPairBN / 2);
+        if (!rc)
+          rc = make_tmap_bf16_2d(&maps[6 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
+                                 (uint64_t)G.ldx, kBK, 16);
+        if (!rc)
+          rc = make_tmap_bf16_2d(&maps[8 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
+                                 (uint64_t)G.ldx, kBK, 64);
+        if (rc) return rc;
+        a.g[g].tma_store = 1;
+      }
+      if (ngroups == 1) {
+        maps[3] = maps[2];
+        maps[5] = maps[4];
+        maps[7] = maps[6];
+        maps[9] = maps[8];
+      }
+      const long ptotal = pu[0] + pu[1];
+      if (ptotal > 0x7fffffffL) return set_error(FUS_E_UNSUPPORTED, "grid too large");
+      a.units0 = (int)pu[0];
+      return epilogue == FUS_EPI_SWIGLU ? launch_pair<FUS_EPI_SWIGLU>(maps, a, ptotal, st)
+                                        : launch_pair<FUS_EPI_BF16>(maps, a, ptotal, st);
+    }
     const int grid = (int)(total < sms ? total : sms);
     for (int g = 0; g < ngroups; ++g) {
       const fus_gemm_group& G = groups[g];

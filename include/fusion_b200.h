@@ -59,6 +59,9 @@ extern "C" {
 #define FUS_GEMM_NO_PERSIST 0x10  /* (first group) keep one tile per CTA; by default wide- */
                                   /* tile launches with many tiles run one persistent CTA  */
                                   /* per SM that overlaps each epilogue with the next loads */
+#define FUS_GEMM_NO_PAIR 0x40     /* (first group) no SM-pair (2-CTA cluster, M = 256)     */
+                                  /* tiles; by default persistent launches with 256-token  */
+                                  /* blocks and dense outputs use them                     */
 
 int fus_version(void);
 const char* fus_last_error(void);

@@ -217,3 +217,67 @@ def test_persistent_equals_one_tile_per_cta(bn, epi):
             yref = torch.zeros(R, H, device=DEV)
             yref[s[valid].long()] = ref[valid] * scale[s[valid].long()][:, None]
             assert rel_err(outs[0][0].float().cpu().numpy(), yref.cpu().numpy()) < 1e-2
+
+
+@pytest.mark.parametrize("epi", ["swiglu", "bf16"])
+def test_pair_tiles_ragged_experts(epi):
+    """SM-pair tiles (2-CTA clusters, M = 256, each SM staging half of the token block)
+    give the same bits as the single-CTA persistent kernel and as one tile per CTA, on
+    expert blocks holding 1 .. 256 live tokens (token boxes of 16 / 64 / 128 rows per
+    CTA), with a dense second group (fp32 output on the down projection); and match an
+    fp32 reference."""
+    counts = [1, 17, 100, 130, 256, 300, 513, 40]
+    E, bn = len(counts), 256
+    ids = np.concatenate([np.full(c, e, np.int32) for e, c in enumerate(counts)])
+    ids = np.random.default_rng(5).permutation(ids)[:, None]
+    T = ids.shape[0]
+    s_np, e_np, n_np = O.moe_align_block_size(ids, bn, E)
+    s, eids, ntp = (torch.from_numpy(v).to(DEV) for v in (s_np, e_np, n_np))
+    cap, R = s_np.size, T
+    maxb = cap // bn
+    if epi == "swiglu":
+        H, I = 1024, 4096  # w13: 2I = 8192 weight rows, 16 pair tiles per block
+        x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+        w = (torch.randn(E, 2 * I, H, device=DEV) * 0.03).to(torch.bfloat16)
+        ws = (torch.randn(2 * I, H, device=DEV) * 0.03).to(torch.bfloat16)
+        xs = torch.empty(cap, H, dtype=torch.bfloat16, device=DEV)
+        ops.permute_rows(x, s, ntp, 1, R, xs)
+        w_rows, K, n_out, epi_id, xin, xsh = 2 * I, H, I, ops.FUS_EPI_SWIGLU, xs, x
+        fl = ops.GEMM_SWIGLU_EXACT
+    else:
+        H, I = 6144, 1024  # w2: 6144 weight rows, 24 pair tiles per block
+        a = torch.randn(cap, I, device=DEV).to(torch.bfloat16)
+        a_s = torch.randn(T, I, device=DEV).to(torch.bfloat16)
+        w = (torch.randn(E, H, I, device=DEV) * 0.03).to(torch.bfloat16)
+        ws = (torch.randn(H, I, device=DEV) * 0.03).to(torch.bfloat16)
+        w_rows, K, n_out, epi_id, xin, xsh = H, I, H, ops.FUS_EPI_BF16, a, a_s
+        fl = 0
+    outs = []
+    for flag in (0, ops.GEMM_NO_PAIR, ops.GEMM_NO_PERSIST):
+        o = torch.zeros(cap, n_out, dtype=torch.bfloat16, device=DEV)
+        # the shared group writes fp32 on the down projection (as the prefill block does)
+        o_s = torch.zeros(T, n_out, dtype=torch.bfloat16 if epi == "swiglu" else torch.float32,
+                          device=DEV)
+        fls = fl if epi == "swiglu" else ops.GEMM_OUT_F32
+        gs = [ops.gemm_group(w, xin, o, expert_ids=eids, ntp=ntp, max_blocks=maxb,
+                             row_limit=cap, live_ids=s, live_limit=R, flags=flag | fl),
+              ops.gemm_group(ws, xsh, o_s, max_blocks=-(-T // bn), row_limit=T, flags=fls)]
+        ops.grouped_gemm(gs, w_rows, K, epi_id, bn)
+        outs.append((o, o_s))
+    finish()
+    live = torch.from_numpy(s_np < R).to(DEV)
+    for o, o_s in outs[1:]:
+        assert torch.equal(outs[0][0][live].view(torch.int16), o[live].view(torch.int16))
+        assert torch.equal(outs[0][1], o_s) if o_s.dtype == torch.float32 else \
+            torch.equal(outs[0][1].view(torch.int16), o_s.view(torch.int16))
+    if epi == "swiglu":
+        def fn(xx, ww):
+            h = xx @ ww.t()
+            return torch.nn.functional.silu(h[:, :I]) * h[:, I:]
+    else:
+        def fn(xx, ww):
+            return xx @ ww.t()
+    ref = ref_rows(xin, w, eids.cpu(), bn, fn)
+    assert rel_err(outs[0][0][live].float().cpu().numpy(), ref[live].cpu().numpy()) < 1e-2
+    ref_s = fn(xsh.float(), ws.float())
+    assert rel_err(outs[0][1].float().cpu().numpy(), ref_s.cpu().numpy()) < 1e-2

@@ -47,7 +47,77 @@ class ExpertParallelMoE:
         i = inp.view(torch.int32) if inp.dtype == torch.bfloat16 else inp
         dist.all_to_all_single(o, i, list(out_splits), list(in_splits), group=self.group)
 
-    def forward(self, h: torch.Tensor, r: torch.Tensor) -> dict:
+    def forward(self, h: torch.Tensor, r: torch.Tensor, dispatch: str = "pairs",
+                combine: str = "pairs") -> dict:
+        """Variable-size step (prefill). dispatch="pairs" (default): one x2 row per
+        (token, slot) pair each way (`forward_pairs`). dispatch="dedup": `forward_dedup`."""
+        if dispatch == "pairs":
+            return self.forward_pairs(h, r)
+        if dispatch != "dedup":
+            raise ValueError(f"dispatch={dispatch!r}: 'pairs' or 'dedup'")
+        return self.forward_dedup(h, r, combine)
+
+    def forward_dedup(self, h: torch.Tensor, r: torch.Tensor, combine: str = "pairs") -> dict:
+        """Variable-size step (prefill) with deduplicated dispatch: a token's x2 row travels
+        once to each rank that owns at least one of its experts, with its K slots' local
+        experts (-1 for slots owned elsewhere).
+
+        combine="pairs" (default): the owner returns one expert row per pair, written by its
+          w2 GEMM straight into the order the source expects; the source merges them with
+          the same arithmetic as one GPU.
+        combine="partial": the owner returns one row per (token, rank), the bf16-rounded
+          partial sum_k w_k y_k over its experts (fewer bytes; the extra rounding of the
+          partial can move the output by an ulp)."""
+        if combine not in ("pairs", "partial"):
+            raise ValueError(f"combine={combine!r}: 'pairs' or 'partial'")
+        be = self.be
+        h1, x2, topw, topi = be.route(h, r)
+        T, K = topi.shape
+        W = self.W
+        plan = be.plan_dedup(topi, W, with_pair_pos=combine == "pairs")
+        counts = plan["counts"]  # [rows, pairs] per destination
+        rows_out = [c[0] for c in counts]
+        pairs_out = [c[1] for c in counts]
+        n_send = sum(rows_out)
+        rows, leid, meta = be.pack_dedup(x2, n_send, topi, topw, W, plan, combine)
+        cnt = torch.tensor(counts, dtype=torch.int64, device=rows.device)
+        recv_cnt = torch.empty_like(cnt)
+        self._a2a(recv_cnt, cnt, [1] * W, [1] * W)
+        rc = recv_cnt.tolist()
+        rows_in = [int(c[0]) for c in rc]
+        pairs_in = [int(c[1]) for c in rc]
+        n_in = sum(rows_in)
+        H = rows.shape[1]
+        recv_rows = torch.empty(n_in, H, dtype=rows.dtype, device=rows.device)
+        recv_leid = torch.empty(n_in, K, dtype=leid.dtype, device=rows.device)
+        self._a2a(recv_rows, rows, rows_in, rows_out)
+        self._a2a(recv_leid, leid, rows_in, rows_out)
+        if combine == "pairs":
+            recv_ret = torch.empty(n_in, K, dtype=meta.dtype, device=rows.device)
+            self._a2a(recv_ret, meta, rows_in, rows_out)
+            y = be.local_experts_return(recv_rows, recv_leid, recv_ret, rows_in, pairs_in)
+            ret = torch.empty(sum(pairs_out), H, dtype=y.dtype, device=rows.device)
+            self._a2a(ret, y, pairs_out, pairs_in)
+            ys = be.shared(x2)
+            out = be.merge_pairs(ret, plan["pair_pos"], topw, h1, ys)
+        else:
+            wts, pos = meta
+            recv_w = torch.empty(n_in, K, dtype=wts.dtype, device=rows.device)
+            self._a2a(recv_w, wts, rows_in, rows_out)
+            part = be.local_experts_dedup(recv_rows, recv_leid, recv_w, sum(pairs_in))
+            # returned partials, plus one zero row that the positions of a token's other
+            # slots on the same rank point at
+            ret = torch.empty(n_send + 1, H, dtype=part.dtype, device=rows.device)
+            ret[n_send].zero_()
+            self._a2a(ret[:n_send], part, rows_out, rows_in)
+            ys = be.shared(x2)
+            out = be.merge_dedup(ret, pos, h1, ys)
+        return {"out": out, "h1": h1, "topw": topw, "topi": topi, "rows_in": n_in,
+                "pairs_in": sum(pairs_in)}
+
+    def forward_pairs(self, h: torch.Tensor, r: torch.Tensor) -> dict:
+        """Variable-size step shipping one row per (token, slot) pair (no deduplication);
+        the returned expert rows are merged at the source exactly as on one GPU."""
         be = self.be
         h1, x2, topw, topi = be.route(h, r)
         T, K = topi.shape
@@ -68,7 +138,8 @@ class ExpertParallelMoE:
         y_flat = be.unpack(ret, send_ids, T * K)
         ys = be.shared(x2)
         out = be.merge(y_flat, topw, h1, ys)
-        return {"out": out, "h1": h1, "topw": topw, "topi": topi, "rows_in": n_in}
+        return {"out": out, "h1": h1, "topw": topw, "topi": topi, "rows_in": n_in,
+                "pairs_in": n_in}
 
     def forward_fixed(self, h: torch.Tensor, r: torch.Tensor) -> dict:
         """Small-batch step with fixed split sizes (no host synchronisation, capturable in
@@ -378,6 +449,123 @@ class CudaEPBackend:
         ntp = torch.zeros(1, dtype=torch.int32, device=self.dev)
         ops.moe_align(dest, W, 1, send_ids, eids, ntp)  # stable sort by destination
         return send_ids, leid, [int(v) for v in counts.tolist()]
+
+    def plan_dedup(self, topi, W: int, with_pair_pos: bool = True) -> dict:
+        T, K = topi.shape
+        keys = torch.empty(T * W, dtype=torch.int32, device=self.dev)
+        counts = torch.empty(2 * W, dtype=torch.int32, device=self.dev)
+        ops.ep_plan_dedup(topi, self.E_loc, W, keys, counts)
+        send_ids = torch.empty(T * W, dtype=torch.int32, device=self.dev)
+        eids = torch.empty(T * W, dtype=torch.int32, device=self.dev)
+        ntp = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        ops.moe_align(keys, W, 1, send_ids, eids, ntp)  # stable sort by destination
+        plan = {"send_ids": send_ids, "counts_dev": counts}
+        if with_pair_pos:
+            # each pair's position among the pairs stably sorted by destination = the row
+            # of its expert output in what the owners return
+            R = T * K
+            dest = torch.empty(R, dtype=torch.int32, device=self.dev)
+            leid = torch.empty(R, dtype=torch.int32, device=self.dev)
+            pc = torch.empty(W, dtype=torch.int32, device=self.dev)
+            ops.ep_plan(topi, self.E_loc, W, dest, leid, pc)
+            srt = torch.empty(R, dtype=torch.int32, device=self.dev)
+            e2 = torch.empty(R, dtype=torch.int32, device=self.dev)
+            n2 = torch.zeros(1, dtype=torch.int32, device=self.dev)
+            plan["pair_pos"] = torch.empty(T, K, dtype=torch.int32, device=self.dev)
+            ops.moe_align(dest, W, 1, srt, e2, n2, pos_of=plan["pair_pos"])
+        c = counts.tolist()
+        plan["counts"] = [[c[d], c[W + d]] for d in range(W)]
+        return plan
+
+    def pack_dedup(self, x2, n: int, topi, topw, W: int, plan: dict, combine: str):
+        T, K = topi.shape
+        rows = torch.empty(n, x2.shape[1], dtype=x2.dtype, device=self.dev)
+        leid = torch.empty(n, K, dtype=torch.int32, device=self.dev)
+        if combine == "pairs":
+            ret = torch.empty(n, K, dtype=torch.int32, device=self.dev)
+            ops.ep_pack_dedup(x2, plan["send_ids"], n, W, topi, topw, self.E_loc, rows, leid,
+                              pair_pos=plan["pair_pos"], counts=plan["counts_dev"], ret_out=ret)
+            return rows, leid, ret
+        wts = torch.empty(n, K, dtype=torch.float32, device=self.dev)
+        pos = torch.empty(T, K, dtype=torch.int32, device=self.dev)
+        ops.ep_pack_dedup(x2, plan["send_ids"], n, W, topi, topw, self.E_loc, rows, leid,
+                          w_out=wts, pos=pos, zero_row=n)
+        return rows, leid, (wts, pos)
+
+    def _dedup_layout(self, rows, leid, pairs: int):
+        """Dispatch layout over the received rows' live slots, the permuted token rows and
+        the w13 + SwiGLU GEMM; returns what the w2 launch needs."""
+        n, H = rows.shape
+        K = leid.shape[1]
+        I, E = self.I, self.E_loc
+        R = n * K
+        per = pairs / E
+        bn = 16 if per <= 12 else 32 if per <= 24 else 64 if per <= 48 else 128 if per <= 128 else 256
+        cap = (R + E * (bn - 1) + bn - 1) // bn * bn
+        sorted_ids = torch.empty(cap, dtype=torch.int32, device=self.dev)
+        eids = torch.empty(cap // bn, dtype=torch.int32, device=self.dev)
+        ntp = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        ops.moe_align(leid, E, bn, sorted_ids, eids, ntp)
+        xs = torch.empty(cap, H, dtype=torch.bfloat16, device=self.dev)
+        ops.permute_rows(rows, sorted_ids, ntp, K, R, xs, cap)
+        act = torch.empty(cap, I, dtype=torch.bfloat16, device=self.dev)
+        maxb = min(min(pairs, E) + pairs // bn, cap // bn)
+        ws = ops.GEMM_W_STREAM if per <= bn else 0
+        g = ops.gemm_group(self.w13, xs, act, expert_ids=eids, ntp=ntp, max_blocks=maxb,
+                           row_limit=cap, flags=ops.GEMM_SWIGLU_EXACT | ws,
+                           live_ids=sorted_ids, live_limit=R)
+        ops.grouped_gemm([g], 2 * I, H, ops.FUS_EPI_SWIGLU, bn)
+        return dict(bn=bn, sorted_ids=sorted_ids, eids=eids, ntp=ntp, act=act, maxb=maxb,
+                    ws=ws, R=R)
+
+    def local_experts_return(self, rows, leid, ret_idx, rows_in, pairs_in):
+        """Expert rows of every received pair, in the order the sources expect them back:
+        source s's pairs at [sum(pairs_in[:s]), ...), each at its ret_idx."""
+        n, H = rows.shape
+        P = sum(pairs_in)
+        y = torch.empty(P, H, dtype=torch.bfloat16, device=self.dev)
+        if n == 0 or P == 0:
+            return y
+        L = self._dedup_layout(rows, leid, P)
+        def prefix(v):
+            out = [0]
+            for c in v:
+                out.append(out[-1] + c)
+            return torch.tensor(out, dtype=torch.int32, device=self.dev)
+        rowmap = torch.empty_like(L["sorted_ids"])
+        ops.ep_return_rowmap(L["sorted_ids"], ret_idx, leid.shape[1], prefix(rows_in),
+                             prefix(pairs_in), rowmap)
+        g2 = ops.gemm_group(self.w2, L["act"], y, expert_ids=L["eids"], ntp=L["ntp"],
+                            max_blocks=L["maxb"], row_map=rowmap, row_limit=P, flags=L["ws"],
+                            live_ids=L["sorted_ids"], live_limit=L["R"])
+        ops.grouped_gemm([g2], H, self.I, ops.FUS_EPI_BF16, L["bn"])
+        return y
+
+    def merge_pairs(self, ret, pair_pos, topw, h1, ys):
+        out = torch.empty_like(h1)
+        ops.merge_pos(ret, pair_pos, topw.shape[1], topw, h1, ys, out)
+        return out
+
+    def local_experts_dedup(self, rows, leid, wts, pairs: int):
+        """Partial rows sum_k w_k y_k over this rank's experts of each received row (slots
+        with local expert -1 belong to other ranks)."""
+        n, H = rows.shape
+        out = torch.empty(n, H, dtype=torch.bfloat16, device=self.dev)
+        if n == 0 or pairs == 0:
+            return out
+        L = self._dedup_layout(rows, leid, pairs)
+        y = torch.empty(L["R"], H, dtype=torch.bfloat16, device=self.dev)  # slot order
+        g2 = ops.gemm_group(self.w2, L["act"], y, expert_ids=L["eids"], ntp=L["ntp"],
+                            max_blocks=L["maxb"], row_map=L["sorted_ids"], row_limit=L["R"],
+                            flags=L["ws"], live_ids=L["sorted_ids"], live_limit=L["R"])
+        ops.grouped_gemm([g2], H, self.I, ops.FUS_EPI_BF16, L["bn"])
+        ops.ep_partial_sum(y, leid, wts, out)
+        return out
+
+    def merge_dedup(self, ret, pos, h1, ys):
+        out = torch.empty_like(h1)
+        ops.merge_pos(ret, pos, pos.shape[1], None, h1, ys, out)
+        return out
 
     def pack(self, x2, send_ids, leid, topk: int):
         n = send_ids.numel()

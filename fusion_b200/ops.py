@@ -352,6 +352,40 @@ def ep_unpack(rows, send_ids, n: int, y):
            _stream(), _sp())
 
 
+def ep_plan_dedup(topi, E_loc: int, W: int, keys, counts):
+    """keys[t*W + d] = d if token t has an expert on rank d else -1; counts[d] = rows and
+    counts[W + d] = (token, slot) pairs for rank d."""
+    T, K = topi.shape
+    L.call("fus_ep_plan_dedup", _p(topi), T, K, E_loc, W, _p(keys), _p(counts), _stream(), _sp())
+
+
+def ep_pack_dedup(x, send_ids, n: int, W: int, topi, topw, E_loc: int, rows, leid_out,
+                  pair_pos=None, counts=None, ret_out=None, w_out=None, pos=None,
+                  zero_row: int = 0):
+    """One row per (token, destination) with its K slots' local expert (-1 off that
+    destination); with ret_out, each slot's place in the owner's return rows; with w_out /
+    pos, the partial-sum combine's slot weights and merge positions."""
+    K = topi.shape[1]
+    L.call("fus_ep_pack_dedup", _p(x), _ld(x), x.shape[1], _p(send_ids), n, W, _p(topi),
+           _p(topw), K, E_loc, _p(pair_pos), _p(counts), _p(rows), _ld(rows), _p(leid_out),
+           _p(ret_out), _p(w_out), _p(pos), zero_row, _stream(), _sp())
+
+
+def ep_return_rowmap(sorted_ids, ret_idx, K: int, row_prefix, pair_prefix, rowmap):
+    """Owner's w2 row map into the return buffer (see fus_ep_return_rowmap)."""
+    n = ret_idx.numel() // K
+    W = row_prefix.numel() - 1
+    L.call("fus_ep_return_rowmap", _p(sorted_ids), sorted_ids.numel(), _p(ret_idx), n, K,
+           _p(row_prefix), _p(pair_prefix), W, _p(rowmap), _stream(), _sp())
+
+
+def ep_partial_sum(y, leid, w, out):
+    """out[i] = bf16(sum_j w[i, j] * y[i*K + j] over slots with leid[i, j] >= 0)."""
+    n, K = leid.shape
+    L.call("fus_ep_partial_sum", _p(y), _ld(y), y.shape[1], _p(leid), _p(w), n, K, _p(out),
+           _ld(out), _stream(), _sp())
+
+
 # -------------------------------------------------------------------------------------
 # NVLink peer-memory exchange (CUDA IPC)
 def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:

@@ -415,6 +415,43 @@ int fus_ep_pack(const void* x, long ldx, int H, const int* send_ids, int n, int 
                 const int* leid, void* rows, long ldr, int* leid_out, void* stream, int* status);
 int fus_ep_unpack(const void* rows, long ldr, int H, const int* send_ids, int n, void* y, long ldy,
                   void* stream, int* status);
+/* Deduplicated dispatch (prefill): a token's row travels once to each rank that owns at
+ * least one of its experts (not once per (token, slot) pair).
+ * fus_ep_plan_dedup : keys[t*W + d] = d if token t has an expert on rank d, else -1;
+ *                     counts[2W] = rows, then (token, slot) pairs, per destination
+ *                     (zeroed here). Sorting keys stably (fus_moe_align(keys, T*W, W, 1,
+ *                     ...)) gives send_ids = t*W + d.
+ * fus_ep_pack_dedup : row p (id = send_ids[p] = t*W + d): rows[p] = x[t]; for k < K:
+ *                     leid_out[p*K + k] = local expert of slot k if its expert is on d,
+ *                     else -1 (K <= 32). Optional outputs:
+ *                     ret_out[p*K + k] = the pair's index among this rank's pairs for d
+ *                       (pair_pos: each pair's position in the pairs stably sorted by
+ *                       destination, counts as above; -1 off d);
+ *                     w_out / pos (together): slot weight (0 off d); pos[t*K + k] = p for
+ *                       the first slot of t on d, zero_row for its other slots on d.
+ * fus_ep_return_rowmap: owner side, the w2 row map that writes each received pair's
+ *                     expert row at its place in the return buffer: layout entry x with
+ *                     slot f = sorted_ids[x] < n*K of row i = f / K from source s
+ *                     (row_prefix[s] <= i < row_prefix[s+1]) -> pair_prefix[s] +
+ *                     ret_idx[f]; pads stay >= n*K. row_prefix / pair_prefix: W+1 ints.
+ * fus_ep_partial_sum: owner side, out[i] = bf16(sum_{j: leid[i*K+j] >= 0} w[i*K+j] *
+ *                     y[i*K+j]) in fp32, slot order (y: expert rows in slot order).
+ * Pair combine (exact): the owner returns one expert row per pair, the source merges
+ * with fus_merge_pos(ret, pair_pos, K, topw, h1, shared), as on one GPU. Partial-sum
+ * combine (fewer bytes, the partial is rounded to bf16 before the final sum): one row
+ * per (token, rank) returns and fus_merge_pos(ret, pos, K, w = NULL, h1, shared) with
+ * ret row zero_row zero. */
+int fus_ep_plan_dedup(const int* topi, int T, int K, int E_loc, int W, int* keys, int* counts,
+                      void* stream, int* status);
+int fus_ep_pack_dedup(const void* x, long ldx, int H, const int* send_ids, int n, int W,
+                      const int* topi, const float* topw, int K, int E_loc, const int* pair_pos,
+                      const int* counts, void* rows, long ldr, int* leid_out, int* ret_out,
+                      float* w_out, int* pos, int zero_row, void* stream, int* status);
+int fus_ep_return_rowmap(const int* sorted_ids, int cap, const int* ret_idx, int n, int K,
+                         const int* row_prefix, const int* pair_prefix, int W, int* rowmap,
+                         void* stream, int* status);
+int fus_ep_partial_sum(const void* y, long ldy, int H, const int* leid, const float* w, int n,
+                       int K, void* out, long ldo, void* stream, int* status);
 
 /* Row exchange over NVLink peer memory for the fixed-slot (decode) step, replacing the
  * three all_to_alls with direct peer stores and flag waits. Every rank exports one

@@ -31,6 +31,88 @@ class NumpyEPBackend:
         counts = np.bincount(dest, minlength=W).tolist()
         return torch.from_numpy(send), torch.from_numpy((t % self.E_loc).astype(np.int32)), counts
 
+    def plan_dedup(self, topi, W: int, with_pair_pos: bool = True) -> dict:
+        ti = topi.numpy()
+        T, K = ti.shape
+        dest = ti // self.E_loc
+        keys = np.full((T, W), -1, dtype=np.int64)
+        for t in range(T):
+            for d in set(dest[t].tolist()):
+                keys[t, d] = d
+        flat = keys.reshape(-1)
+        send = np.nonzero(flat >= 0)[0]
+        send = send[np.argsort(flat[send], kind="stable")].astype(np.int32)
+        counts = [[int((keys[:, d] == d).sum()), int((dest == d).sum())] for d in range(W)]
+        plan = {"send_ids": torch.from_numpy(send), "counts": counts}
+        if with_pair_pos:
+            order = np.argsort(dest.reshape(-1), kind="stable")
+            pp = np.empty(T * K, dtype=np.int32)
+            pp[order] = np.arange(T * K, dtype=np.int32)
+            plan["pair_pos"] = torch.from_numpy(pp.reshape(T, K))
+        return plan
+
+    def pack_dedup(self, x2, n: int, topi, topw, W: int, plan: dict, combine: str):
+        ti, tw = topi.numpy(), topw.numpy()
+        T, K = ti.shape
+        leid = np.full((n, K), -1, dtype=np.int32)
+        ret = np.full((n, K), -1, dtype=np.int32)
+        wts = np.zeros((n, K), dtype=np.float32)
+        pos = np.full((T, K), n, dtype=np.int32)
+        ids = plan["send_ids"].numpy()
+        base = np.concatenate([[0], np.cumsum([c[1] for c in plan["counts"]])])
+        for p, i in enumerate(ids):
+            t, d = divmod(int(i), W)
+            first = True
+            for k in range(K):
+                if ti[t, k] // self.E_loc == d:
+                    leid[p, k] = ti[t, k] % self.E_loc
+                    wts[p, k] = tw[t, k]
+                    if combine == "pairs":
+                        ret[p, k] = int(plan["pair_pos"][t, k]) - base[d]
+                    if first:
+                        pos[t, k] = p
+                        first = False
+        rows = x2[torch.from_numpy(ids.astype(np.int64) // W)].contiguous()
+        if combine == "pairs":
+            return rows, torch.from_numpy(leid), torch.from_numpy(ret)
+        return rows, torch.from_numpy(leid), (torch.from_numpy(wts), torch.from_numpy(pos))
+
+    def local_experts_return(self, rows, leid, ret_idx, rows_in, pairs_in):
+        n, K = leid.shape
+        y = torch.zeros(sum(pairs_in), rows.shape[1], dtype=torch.bfloat16)
+        rp = np.concatenate([[0], np.cumsum(rows_in)])
+        pp = np.concatenate([[0], np.cumsum(pairs_in)])
+        lid, ri = leid.numpy(), ret_idx.numpy()
+        for i in range(n):
+            s = int(np.searchsorted(rp, i, side="right") - 1)
+            for j in range(K):
+                if lid[i, j] >= 0:
+                    y[pp[s] + ri[i, j]] = self.local_experts(rows[i:i + 1], leid[i, j:j + 1])[0]
+        return y
+
+    def merge_pairs(self, ret, pair_pos, topw, h1, ys):
+        T, K = topw.shape
+        y = ret.float().numpy()[pair_pos.numpy().astype(np.int64)]
+        acc = (y * topw.numpy()[..., None]).sum(1) + h1.float().numpy() + ys.numpy()
+        return _bf(acc)
+
+    def local_experts_dedup(self, rows, leid, wts, pairs: int):
+        n, K = leid.shape
+        lid, w = leid.numpy(), wts.numpy()
+        out = np.zeros((n, rows.shape[1]), dtype=np.float32)
+        for i in range(n):
+            for j in range(K):
+                if lid[i, j] < 0:
+                    continue
+                y = self.local_experts(rows[i:i + 1], leid[i, j:j + 1]).float().numpy()[0]
+                out[i] += w[i, j] * y
+        return _bf(out)
+
+    def merge_dedup(self, ret, pos, h1, ys):
+        r = ret.float().numpy()
+        acc = r[pos.numpy().astype(np.int64)].sum(1) + h1.float().numpy() + ys.numpy()
+        return _bf(acc)
+
     def pack(self, x2, send_ids, leid, topk: int):
         s = send_ids.long()
         return x2[s // topk].contiguous(), leid[s].contiguous()

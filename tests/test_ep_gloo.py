@@ -32,7 +32,7 @@ def _weights(world: int, rank: int):
     return d, full, loc
 
 
-def _worker(rank: int, world: int, port: int, T_by_rank, q, fixed=False):
+def _worker(rank: int, world: int, port: int, T_by_rank, q, mode="dedup"):
     sys.path.insert(0, str(HERE))
     sys.path.insert(0, str(HERE.parent))
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -48,7 +48,10 @@ def _worker(rank: int, world: int, port: int, T_by_rank, q, fixed=False):
         T = T_by_rank[rank]
         h, r = synth.make_inputs(50 + rank, T, d, "cpu")
         ep = ExpertParallelMoE(NumpyEPBackend(loc, d.E, world, rank, d.topk))
-        res = ep.forward_fixed(h, r) if fixed else ep(h, r)
+        res = {"dedup": ep.forward_dedup,
+               "partial": lambda h, r: ep.forward_dedup(h, r, "partial"),
+               "pairs": ep.forward, "fixed": ep.forward_fixed}[mode](h, r)
+        res.setdefault("pairs_in", None)
         res.setdefault("rows_in", None)
         f = {k: (v.float().numpy() if v is not None else None) for k, v in full.items()}
         ref = O.moe_block(h.float().numpy(), r.float().numpy(), f["gamma"], f["gate_w"],
@@ -58,7 +61,7 @@ def _worker(rank: int, world: int, port: int, T_by_rank, q, fixed=False):
         err = 0.0 if T == 0 else float(np.abs(out - ref["out"]).max() /
                                        max(np.abs(ref["out"]).max(), 1e-6))
         q.put((rank, err, bool(np.array_equal(res["topi"].numpy(), ref["topk_ids"])),
-               res["rows_in"]))
+               res["pairs_in"], res["rows_in"]))
     finally:
         dist.destroy_process_group()
 
@@ -69,13 +72,19 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("T_by_rank,fixed", [((5, 5), False), ((7, 1), False), ((3, 0), False),
-                                              ((4, 4), True), ((1, 1), True)])
-def test_ep_two_gloo_ranks_match_oracle(T_by_rank, fixed):
+@pytest.mark.parametrize("T_by_rank,mode", [((5, 5), "dedup"), ((7, 1), "dedup"),
+                                             ((3, 0), "dedup"), ((5, 5), "partial"),
+                                             ((0, 2), "partial"), ((5, 5), "pairs"),
+                                             ((3, 0), "pairs"), ((4, 4), "fixed"),
+                                             ((1, 1), "fixed")])
+def test_ep_two_gloo_ranks_match_oracle(T_by_rank, mode):
+    """pairs (the default): one row per (token, slot) both ways; dedup: one row per
+    (token, owning rank) out, one expert row per pair back; partial: the same dispatch,
+    one partial-sum row per (token, rank) back; fixed: fixed slot blocks (decode)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, T_by_rank, q, fixed))
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, T_by_rank, q, mode))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -87,7 +96,9 @@ def test_ep_two_gloo_ranks_match_oracle(T_by_rank, fixed):
     total_pairs = sum(T_by_rank) * D["topk"]
     if None not in [r[3] for r in res]:
         assert sum(r[3] for r in res) == total_pairs  # every pair processed exactly once
-    for rank, err, ids_ok, _ in res:
+    if mode in ("dedup", "partial"):  # at most one row per (token, rank)
+        assert sum(r[4] for r in res) <= min(total_pairs, 2 * sum(T_by_rank))
+    for rank, err, ids_ok, _, _ in res:
         if T_by_rank[rank] == 0:
             continue
         assert ids_ok, rank

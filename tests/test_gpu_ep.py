@@ -1,9 +1,11 @@
-"""GPU tests of expert parallelism: the plan/pack/unpack kernels against their
-definitions, the EP path on one rank against the single-GPU block, and (with two GPUs
-visible) two NCCL ranks against the single-GPU block on the same tokens."""
+"""GPU tests of expert parallelism: the plan/pack/unpack kernels (per pair and
+deduplicated) against their definitions, the EP path on one rank against the single-GPU
+block, and (with two GPUs visible) two NCCL ranks against the single-GPU block on the
+same tokens."""
 
 from __future__ import annotations
 
+import datetime
 import os
 import socket
 import sys
@@ -57,6 +59,124 @@ def test_ep_plan_pack_unpack_kernels():
     assert torch.equal(y, x.repeat_interleave(K, 0))  # unpack inverts pack
 
 
+def test_ep_dedup_plan_pack_partial_kernels():
+    """Deduplicated dispatch: keys / counts / send order / packed rows and slot metadata /
+    merge positions bit-exact against their definitions; the owner's partial sum within
+    bf16 rounding of the fp32 sum."""
+    T, K, E, W, H = 300, 8, 256, 4, 6144
+    rng = np.random.default_rng(2)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    topi = torch.from_numpy(ids).to(DEV)
+    topw = torch.rand(T, K, device=DEV)
+    E_loc = E // W
+    keys = torch.empty(T * W, dtype=torch.int32, device=DEV)
+    counts = torch.empty(2 * W, dtype=torch.int32, device=DEV)
+    ops.ep_plan_dedup(topi, E_loc, W, keys, counts)
+    send = torch.empty(T * W, dtype=torch.int32, device=DEV)
+    eids = torch.empty_like(send)
+    ntp = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.moe_align(keys, W, 1, send, eids, ntp)
+    finish()
+    dest = ids // E_loc
+    on = np.zeros((T, W), bool)
+    for t in range(T):
+        on[t, dest[t]] = True
+    ref_keys = np.where(on, np.arange(W)[None, :], -1).reshape(-1)
+    assert np.array_equal(keys.cpu().numpy(), ref_keys)
+    n = int(on.sum())
+    assert np.array_equal(counts.cpu().numpy(),
+                          np.concatenate([on.sum(0), np.bincount(dest.reshape(-1), minlength=W)]))
+    ref_send = np.nonzero(ref_keys >= 0)[0]
+    ref_send = ref_send[np.argsort(ref_keys[ref_send], kind="stable")]
+    assert int(ntp.item()) == n
+    assert np.array_equal(send[:n].cpu().numpy(), ref_send)
+    # each pair's position among the pairs stably sorted by destination
+    pdest = torch.empty(T * K, dtype=torch.int32, device=DEV)
+    pleid, pc = torch.empty_like(pdest), torch.empty(W, dtype=torch.int32, device=DEV)
+    ops.ep_plan(topi, E_loc, W, pdest, pleid, pc)
+    srt, e2 = torch.empty_like(pdest), torch.empty_like(pdest)
+    pair_pos = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    ops.moe_align(pdest, W, 1, srt, e2, torch.zeros(1, dtype=torch.int32, device=DEV),
+                  pos_of=pair_pos)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    rows = torch.empty(n, H, dtype=torch.bfloat16, device=DEV)
+    leid = torch.empty(n, K, dtype=torch.int32, device=DEV)
+    ret = torch.empty(n, K, dtype=torch.int32, device=DEV)
+    ops.ep_pack_dedup(x, send, n, W, topi, topw, E_loc, rows, leid, pair_pos=pair_pos,
+                      counts=counts, ret_out=ret)
+    rows2, leid2 = torch.empty_like(rows), torch.empty_like(leid)
+    wts = torch.empty(n, K, dtype=torch.float32, device=DEV)
+    pos = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    ops.ep_pack_dedup(x, send, n, W, topi, topw, E_loc, rows2, leid2, w_out=wts, pos=pos,
+                      zero_row=n)
+    finish()
+    tw = topw.cpu().numpy()
+    order = np.argsort(dest.reshape(-1), kind="stable")
+    ref_pp = np.empty(T * K, np.int64)
+    ref_pp[order] = np.arange(T * K)
+    ref_pp = ref_pp.reshape(T, K)
+    assert np.array_equal(pair_pos.cpu().numpy(), ref_pp)
+    base = np.concatenate([[0], np.cumsum(np.bincount(dest.reshape(-1), minlength=W))])
+    ref_leid = np.full((n, K), -1, np.int32)
+    ref_ret = np.full((n, K), -1, np.int32)
+    ref_w = np.zeros((n, K), np.float32)
+    ref_pos = np.full((T, K), n, np.int32)
+    for p, i in enumerate(ref_send):
+        t, d = divmod(int(i), W)
+        mine = np.nonzero(dest[t] == d)[0]
+        ref_leid[p, mine] = ids[t, mine] % E_loc
+        ref_ret[p, mine] = ref_pp[t, mine] - base[d]
+        ref_w[p, mine] = tw[t, mine]
+        ref_pos[t, mine[0]] = p
+    assert torch.equal(rows, x[torch.from_numpy(ref_send // W).to(DEV)])
+    assert torch.equal(rows2, rows) and torch.equal(leid2, leid)
+    assert np.array_equal(leid.cpu().numpy(), ref_leid)
+    assert np.array_equal(ret.cpu().numpy(), ref_ret)
+    assert np.array_equal(wts.cpu().numpy(), ref_w)
+    assert np.array_equal(pos.cpu().numpy(), ref_pos)
+    # owner: rows arriving from 3 sources (this batch split 40 / 0 / rest rows), the
+    # row map sends slot f of row i to pair_prefix[s] + ret[f]; pads stay past the rows
+    rows_in = [40, 0, n - 40]
+    pairs_in = [int((ref_leid[:40] >= 0).sum()), 0, int((ref_leid[40:] >= 0).sum())]
+    rp = torch.tensor([0, 40, 40, n], dtype=torch.int32, device=DEV)
+    pp = torch.tensor([0, pairs_in[0], pairs_in[0], sum(pairs_in)], dtype=torch.int32,
+                      device=DEV)
+    # each source's return indices: a permutation of its own pairs
+    ret_src = np.full((n, K), -1, np.int32)
+    for lo, hi in ((0, 40), (40, n)):
+        live = ref_leid[lo:hi] >= 0
+        blk = ret_src[lo:hi]
+        blk[live] = rng.permutation(int(live.sum()))
+    flat_live = np.nonzero(ref_leid.reshape(-1) >= 0)[0]
+    sorted_ids = np.concatenate([flat_live, np.full(5, n * K)]).astype(np.int32)
+    rowmap = torch.empty(sorted_ids.size, dtype=torch.int32, device=DEV)
+    ops.ep_return_rowmap(torch.from_numpy(sorted_ids).to(DEV),
+                         torch.from_numpy(ret_src).to(DEV), K, rp, pp, rowmap)
+    finish()
+    ref_map = []
+    for f in sorted_ids:
+        if f >= n * K:
+            ref_map.append(int(f))
+            continue
+        i = f // K
+        src = 0 if i < 40 else 2
+        ref_map.append(int([0, pairs_in[0], pairs_in[0]][src] + ret_src.reshape(-1)[f]))
+    assert np.array_equal(rowmap.cpu().numpy(), np.array(ref_map))
+    assert ops.read_status() == 0
+    # owner: partial = bf16(sum over its slots of w * y); hole rows hold NaN and must be
+    # skipped, not multiplied by a zero weight
+    y = torch.randn(n * K, H, device=DEV).to(torch.bfloat16)
+    y[torch.from_numpy(np.nonzero(ref_leid.reshape(-1) < 0)[0]).to(DEV)] = float("nan")
+    part = torch.empty(n, H, dtype=torch.bfloat16, device=DEV)
+    ops.ep_partial_sum(y, leid, wts, part)
+    finish()
+    yf = torch.nan_to_num(y.float().view(n, K, H), nan=0.0)
+    ref = (yf * torch.from_numpy(ref_w).to(DEV)[..., None]).sum(1)
+    got = part.float()
+    assert torch.isfinite(got).all()
+    assert float((got - ref).abs().max()) <= float(ref.abs().max()) * 2 ** -7
+
+
 def test_align_skips_holes():
     rng = np.random.default_rng(5)
     ids = rng.integers(-1, 64, size=(300, 1)).astype(np.int32)  # -1: holes
@@ -97,6 +217,20 @@ def test_ep_single_rank_matches_block(T, fixed):
     assert torch.equal(res["topi"], ref.topi)
     assert torch.equal(res["h1"].view(torch.int16), ref.h1.view(torch.int16))
     _parity(res["out"], ref.out)
+    if not fixed:
+        # deduplicated dispatch (one row per token here) returning one expert row per
+        # pair merges exactly like the per-pair exchange
+        res_dd = ep.forward_dedup(h, r)
+        finish()
+        assert torch.equal(res_dd["out"].view(torch.int16), res["out"].view(torch.int16))
+        assert res_dd["rows_in"] == T and res_dd["pairs_in"] == T * D.topk
+        # partial-sum combine: the owner's bf16 partial adds a rounding before the final
+        # sum, so an element may move by up to an ulp of itself
+        res_part = ep.forward_dedup(h, r, combine="partial")
+        finish()
+        o, rr = res_part["out"].float(), ref.out.float()
+        rms = float(rr.pow(2).mean().sqrt())
+        assert bool(((o - rr).abs() <= 1e-2 * rms + rr.abs() * 2 ** -7).all())
     if fixed:
         # the NVLink exchange (here its loopback on one rank) gives the same bits
         x = P2PExchange(T * D.topk, D.H, DEV)
@@ -151,8 +285,11 @@ def _two_rank_worker(rank, port, q):
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
+    # a collective that waits longer than this ends the rank with an error instead of
+    # holding the test
     dist.init_process_group("nccl", rank=rank, world_size=2,
-                            device_id=torch.device("cuda", rank))
+                            device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=120))
     try:
         w = shard_weights(404, rank, 2, D, "cuda")
         be = CudaEPBackend(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"],
@@ -202,12 +339,15 @@ def test_ep_two_nccl_ranks_match_block():
     for p in ps:
         p.start()
     # drain before joining: a child cannot exit while its result is still in the pipe
-    outs = dict(q.get(timeout=240) for _ in range(2))
-    for p in ps:
-        p.join(timeout=60)
-        if p.is_alive():  # results are in; do not let a slow teardown hold the test
-            p.terminate()
-            p.join(timeout=10)
+    try:
+        outs = dict(q.get(timeout=240) for _ in range(2))
+        for p in ps:
+            p.join(timeout=60)
+    finally:
+        for p in ps:  # results are in (or never came): do not let a child hold the test
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
     w = synth.make_block_weights(404, D, DEV)
     blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"])
     for rank in range(2):

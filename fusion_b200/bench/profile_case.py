@@ -13,6 +13,9 @@ prefill: 16 experts x 256 tokens each (the per-expert load of T=8192 over 256 ex
 prefill32: the same on 32 experts (2.4 GB of weights; several tiles per SM, so the
          persistent kernel's steady state dominates rather than its tail).
 block<T>: the whole MoE block (MoEBlock.forward, seeded GLM-5.2 weights) on T tokens.
+pairab <per> <reps> [E]: E experts (default 32) with `per` tokens each (balanced layout,
+         256-token blocks), the prefill w13+SwiGLU and w2 launches with SM-pair tiles and
+         with single-CTA persistent tiles (FUS_GEMM_NO_PAIR), interleaved rep by rep.
 Each launch is timed with CUDA events; the line printed gives us and TB/s or TF/s.
 """
 
@@ -43,6 +46,55 @@ def block_case(T: int, reps: int) -> None:
     ops.check_status()
     ts = [ev[i].elapsed_time(ev[i + 1]) * 1e3 for i in range(reps)]
     print(f"block T={T}: " + " ".join(f"{t:.0f}" for t in ts) + " us per call")
+
+
+def pair_ab(per: int, reps: int, E: int = 32) -> None:
+    H, I, K = 6144, 2048, 8
+    w13 = synth.make("w13", (E, 2 * I, H), 1, "cuda")
+    w2 = synth.make("w2", (E, H, I), 1, "cuda")
+    T, bn = per * E // K, 256
+    ids = (torch.arange(T * K, device="cuda") % E).view(T, K).to(torch.int32)
+    R = T * K
+    cap = (R + E * (bn - 1) + bn - 1) // bn * bn
+    s = torch.empty(cap, dtype=torch.int32, device="cuda")
+    e = torch.empty(cap // bn, dtype=torch.int32, device="cuda")
+    n = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.moe_align(ids, E, bn, s, e, n, flags=ops.ALIGN_BALANCED)
+    x = synth.make("h", (T, H), 1, "cuda")
+    xs = torch.empty(cap, H, dtype=torch.bfloat16, device="cuda")
+    ops.permute_rows(x, s, n, K, R, xs, cap)
+    act = torch.empty(cap, I, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(cap, H, dtype=torch.bfloat16, device="cuda")
+    maxb = min(R, E) + R // bn
+
+    def launch(flag):
+        g13 = [ops.gemm_group(w13, xs, act, expert_ids=e, ntp=n, max_blocks=maxb,
+                              row_limit=cap, flags=ops.GEMM_SWIGLU_EXACT | flag, live_ids=s,
+                              live_limit=R)]
+        g2 = [ops.gemm_group(w2, act, y, expert_ids=e, ntp=n, max_blocks=maxb, row_limit=cap,
+                             live_ids=s, live_limit=R, flags=flag)]
+        return (lambda: ops.grouped_gemm(g13, 2 * I, H, ops.FUS_EPI_SWIGLU, bn),
+                lambda: ops.grouped_gemm(g2, H, I, ops.FUS_EPI_BF16, bn))
+
+    variants = {"pair": launch(0), "single": launch(ops.GEMM_NO_PAIR)}
+    tim = {}
+    for _ in range(reps):
+        for nm, (a13, a2) in variants.items():
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+            a13()
+            ev[1].record()
+            a2()
+            ev[2].record()
+            tim.setdefault(nm, []).append(ev)
+    torch.cuda.synchronize()
+    ops.check_status()
+    f13, f2 = 2 * R * H * 2 * I, 2 * R * I * H
+    for nm, v in tim.items():
+        t13 = sorted(x[0].elapsed_time(x[1]) for x in v)[len(v) // 2]
+        t2 = sorted(x[1].elapsed_time(x[2]) for x in v)[len(v) // 2]
+        print(f"per={per} {nm}: w13 {t13 * 1e3:.1f} us {f13 / t13 / 1e9:.0f} TF/s; "
+              f"w2 {t2 * 1e3:.1f} us {f2 / t2 / 1e9:.0f} TF/s")
 
 
 def main(case: str, reps: int = 3) -> None:
@@ -115,4 +167,8 @@ def main(case: str, reps: int = 3) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "decode", int(sys.argv[2]) if len(sys.argv) > 2 else 3)
+    if len(sys.argv) > 1 and sys.argv[1] == "pairab":
+        pair_ab(int(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4]) if len(sys.argv) > 4 else 32)
+    else:
+        main(sys.argv[1] if len(sys.argv) > 1 else "decode",
+             int(sys.argv[2]) if len(sys.argv) > 2 else 3)

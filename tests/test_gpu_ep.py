@@ -290,33 +290,43 @@ def _two_rank_worker(rank, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=2,
                             device_id=torch.device("cuda", rank),
                             timeout=datetime.timedelta(seconds=120))
+
+    def stage(name):  # progress on stderr: a stuck rank shows where it stopped
+        print(f"[two-rank test, rank {rank}] {name}", file=sys.stderr, flush=True)
+
     try:
+        stage("init done")
         w = shard_weights(404, rank, 2, D, "cuda")
         be = CudaEPBackend(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"],
                            w["w2s"], E=D.E, rank=rank)
         ep = ExpertParallelMoE(be)
         h, r = synth.make_inputs(70 + rank, 24, D, "cuda")
         out = ep(h, r)["out"]
+        stage("prefill step (all_to_all) done")
         h2, r2 = synth.make_inputs(90 + rank, 2, D, "cuda")
         g = EPDecodeGraph(ep, 2, D.H, "cuda", exchange="nccl")  # all_to_all in a CUDA graph
         g.h.copy_(h2)
         g.r.copy_(r2)
         out2 = g.replay()
+        stage("decode graph (all_to_all) done")
         gp = EPDecodeGraph(ep, 2, D.H, "cuda", exchange="p2p")  # NVLink peer stores
         gp.h.copy_(h2)
         gp.r.copy_(r2)
         for _ in range(3):
             out3 = gp.replay()
+        stage("decode graph (NVLink) done")
         st = EPDecodeStep(be, 2).capture()  # one library call per step, graphed
         st.h.copy_(h2)
         st.r.copy_(r2)
         for _ in range(3):
             out4 = st.replay()
+        stage("decode step (one call) done")
         torch.cuda.synchronize()
         ops.check_status()
         same = bool(torch.equal(out2.view(torch.int16), out3.view(torch.int16)) and
                     torch.equal(out2.view(torch.int16), out4.view(torch.int16)))
         q.put((rank, (out.float().cpu().numpy(), out2.float().cpu().numpy(), same)))
+        stage("results sent")
         del g  # the graph holds NCCL work: release it before the communicator
         torch.cuda.synchronize()
         gp.close()

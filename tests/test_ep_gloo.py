@@ -1,4 +1,4 @@
-"""Expert-parallel exchange on 2 gloo CPU ranks (world_size 2): each rank owns half of
+"""Expert-parallel exchange on 2 and 4 gloo CPU ranks: each rank owns 1/W of
 the experts, routes its own tokens, ships rows to the owners and merges what comes back.
 Each rank's output must equal the single-process oracle of the whole block on its
 tokens (reference composition glm52/bench/bench_layer.py:365-374)."""
@@ -76,19 +76,22 @@ def _free_port() -> int:
                                              ((3, 0), "dedup"), ((5, 5), "partial"),
                                              ((0, 2), "partial"), ((5, 5), "pairs"),
                                              ((3, 0), "pairs"), ((4, 4), "fixed"),
-                                             ((1, 1), "fixed")])
-def test_ep_two_gloo_ranks_match_oracle(T_by_rank, mode):
+                                             ((1, 1), "fixed"), ((3, 2, 0, 4), "dedup"),
+                                             ((3, 2, 0, 4), "pairs"),
+                                             ((2, 2, 2, 2), "partial")])
+def test_ep_gloo_ranks_match_oracle(T_by_rank, mode):
     """pairs (the default): one row per (token, slot) both ways; dedup: one row per
     (token, owning rank) out, one expert row per pair back; partial: the same dispatch,
-    one partial-sum row per (token, rank) back; fixed: fixed slot blocks (decode)."""
+    one partial-sum row per (token, rank) back; fixed: fixed slot blocks (decode). World size = len(T_by_rank)."""
+    W = len(T_by_rank)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, T_by_rank, q, mode))
-             for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, W, port, T_by_rank, q, mode))
+             for r in range(W)]
     for p in procs:
         p.start()
-    res = sorted(q.get(timeout=120) for _ in range(2))  # drain before joining
+    res = sorted(q.get(timeout=180) for _ in range(W))  # drain before joining
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0, f"rank exited with {p.exitcode}"
@@ -97,7 +100,7 @@ def test_ep_two_gloo_ranks_match_oracle(T_by_rank, mode):
     if None not in [r[3] for r in res]:
         assert sum(r[3] for r in res) == total_pairs  # every pair processed exactly once
     if mode in ("dedup", "partial"):  # at most one row per (token, rank)
-        assert sum(r[4] for r in res) <= min(total_pairs, 2 * sum(T_by_rank))
+        assert sum(r[4] for r in res) <= min(total_pairs, W * sum(T_by_rank))
     for rank, err, ids_ok, _, _ in res:
         if T_by_rank[rank] == 0:
             continue

@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--regimes", default=",".join(REGIMES),
                     help="extra T values measured besides the headline ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefetch-shared", action="store_true",
+                    help="decode: the front end pulls the shared expert's weights into L2")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1 decode row exchange: NVLink peer stores or NCCL all_to_all")
     return ap.parse_args()
@@ -387,7 +389,8 @@ def main() -> None:
 
     dims = synth.Dims()
     w = synth.make_block_weights(SEED, dims, "cuda")
-    blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"])
+    blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"],
+                   prefetch_shared=args.prefetch_shared)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     pk = traffic.peaks()
 
@@ -564,7 +567,9 @@ def main() -> None:
                        "topk": dims.topk, "block_n": head["block_n"],
                        "l2": "flushed by a 512 MB write before every timed step",
                        "parallelism": "single",
-                       "timing": "CUDA-graph replay of the 8-launch block, CUDA events"},
+                       "prefetch_shared": bool(args.prefetch_shared),
+                       "timing": f"CUDA-graph replay of the {launches_per_step(HEADLINE_T)}"
+                                 "-launch block, CUDA events"},
             "us_per_block": head["us_per_block"],
             "block_roofline": {"roofline_us": head["roofline_us"],
                                "frac": head["roofline_frac"],

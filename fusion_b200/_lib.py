@@ -64,6 +64,9 @@ class MergeSpec(C.Structure):
     ]
 
 
+FUS_BLOCK_PREFETCH_SHARED = 0x1
+
+
 class BlockDesc(C.Structure):
     """Mirror of ``fus_moe_block_desc``."""
 
@@ -85,6 +88,7 @@ class BlockDesc(C.Structure):
         ("w2s", vp),
         ("n_group", i32),
         ("topk_group", i32),
+        ("flags", i32),
     ]
 
 

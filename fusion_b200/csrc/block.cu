@@ -148,13 +148,16 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
 
   int rc;
   const bool small = small_path(d, T);
+  const bool pf_shared = shared && (d->flags & FUS_BLOCK_PREFETCH_SHARED);
   if (small) {
     // decode: norm + router + top-k + layout in one launch; it also clears the merge
     // counters, so the down projection needs no separate reset
     if ((rc = route_small_launch(h, r, d->gamma, d->eps, d->wa, d->nplanes, d->bias, T, H, E, K,
                                  d->routed_scale, d->renorm, d->n_group, d->topk_group, h1, x2,
                                  partial, topw, topi, block_n, sorted, L.cap, eids, L.blocks_cap,
-                                 ntp, done, counters, T * L.tiles, stream, status)))
+                                 ntp, done, counters, T * L.tiles, stream, status,
+                                 pf_shared ? d->w13s : nullptr, 2L * I * H * 2,
+                                 pf_shared ? d->w2s : nullptr, (long)H * I * 2)))
       return rc;
   } else {
     if ((rc = fus_add_rmsnorm(h, H, r, H, d->gamma, h1, H, x2, H, T, H, d->eps, 1, 1, stream,

@@ -266,6 +266,11 @@ FUS_DEVICE void st_global_v4_hint(void* p, uint4 v, uint64_t policy) {
                : "memory");
 }
 
+// asynchronous prefetch of `bytes` (a multiple of 16, 16-byte aligned start) into L2
+FUS_DEVICE void l2_prefetch_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 FUS_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1,
                             uint64_t policy) {
   asm volatile(

@@ -383,7 +383,13 @@ typedef struct fus_moe_block_desc {
   const void* w2s;    /* shared expert [H, I] bf16 or NULL        */
   int n_group;        /* noaux_tc groups (0 or 1: none; GLM-5.2)  */
   int topk_group;     /* groups kept when n_group > 1             */
+  int flags;          /* FUS_BLOCK_* options (0: none)            */
 } fus_moe_block_desc;
+
+/* Block option: at decode, the front end (norm + router + top-k) also asks for the shared
+ * expert's weights in L2, so that the expert GEMMs read that part from L2 instead of
+ * HBM (the front end is latency-bound and leaves HBM idle). */
+#define FUS_BLOCK_PREFETCH_SHARED 0x1
 
 int fus_moe_block_pick_block_n(int T, int E, int topk);
 size_t fus_moe_block_workspace(const fus_moe_block_desc* d, int T, int block_n);

@@ -16,6 +16,8 @@ block<T>: the whole MoE block (MoEBlock.forward, seeded GLM-5.2 weights) on T to
 pairab <per> <reps> [E]: E experts (default 32) with `per` tokens each (balanced layout,
          256-token blocks), the prefill w13+SwiGLU and w2 launches with SM-pair tiles and
          with single-CTA persistent tiles (FUS_GEMM_NO_PAIR), interleaved rep by rep.
+         per = "real": seeded counts in 202..311 per expert, the spread of the seeded
+         T=8192 routing over 256 experts (about half the experts take two blocks).
 Each launch is timed with CUDA events; the line printed gives us and TB/s or TF/s.
 """
 
@@ -48,12 +50,24 @@ def block_case(T: int, reps: int) -> None:
     print(f"block T={T}: " + " ".join(f"{t:.0f}" for t in ts) + " us per call")
 
 
-def pair_ab(per: int, reps: int, E: int = 32) -> None:
+def pair_ab(per, reps: int, E: int = 32) -> None:
+    import numpy as np
+
     H, I, K = 6144, 2048, 8
     w13 = synth.make("w13", (E, 2 * I, H), 1, "cuda")
     w2 = synth.make("w2", (E, H, I), 1, "cuda")
-    T, bn = per * E // K, 256
-    ids = (torch.arange(T * K, device="cuda") % E).view(T, K).to(torch.int32)
+    bn = 256
+    if per == "real":
+        rng = np.random.default_rng(8192)
+        counts = rng.integers(202, 312, E)
+        flat = np.repeat(np.arange(E), counts)
+        flat = rng.permutation(flat)[: len(flat) // K * K]
+        T = len(flat) // K
+        ids = torch.from_numpy(flat.astype(np.int32)).view(T, K).cuda()
+    else:
+        per = int(per)
+        T = per * E // K
+        ids = (torch.arange(T * K, device="cuda") % E).view(T, K).to(torch.int32)
     R = T * K
     cap = (R + E * (bn - 1) + bn - 1) // bn * bn
     s = torch.empty(cap, dtype=torch.int32, device="cuda")
@@ -168,7 +182,7 @@ def main(case: str, reps: int = 3) -> None:
 
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "pairab":
-        pair_ab(int(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4]) if len(sys.argv) > 4 else 32)
+        pair_ab(sys.argv[2], int(sys.argv[3]), int(sys.argv[4]) if len(sys.argv) > 4 else 32)
     else:
         main(sys.argv[1] if len(sys.argv) > 1 else "decode",
              int(sys.argv[2]) if len(sys.argv) > 2 else 3)

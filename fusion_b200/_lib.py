@@ -150,6 +150,7 @@ SIGNATURES: dict[str, tuple] = {
     "fus_seed": (i32, [vp, i64, vp, i64, i32, i32, i32, vp, vp]),
     "fus_moe_block_pick_block_n": (i32, [i32, i32, i32]),
     "fus_moe_block_workspace": (sz, [C.POINTER(BlockDesc), i32, i32]),
+    "fus_moe_block_check": (i32, [C.POINTER(BlockDesc), i32, i32, sz]),
     "fus_moe_block_forward": (
         i32,
         [C.POINTER(BlockDesc), vp, vp, i32, i32, vp, vp, vp, vp, vp, sz, vp, vp],

@@ -287,15 +287,9 @@ int moe_align_small_after_flags(const int* flags, const int* epoch, int W, const
                                 int* status) {
   if (numel > kAlignSmallMax || E < 1 || E > kAlignMaxE || W > kAlignThreads)
     return set_error(FUS_E_UNSUPPORTED, "moe_align_after_flags: numel=%d E=%d W=%d", numel, E, W);
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(align_small_after_flags_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)small_smem_bytes(kAlignMaxE));
-  });
-  if (attr_err != cudaSuccess)
-    return set_error(FUS_E_LAUNCH, "moe_align attr: %s", cudaGetErrorString(attr_err));
+  if (int rc = ensure_smem_attr((const void*)align_small_after_flags_kernel,
+                                 (int)small_smem_bytes(kAlignMaxE), "moe_align_after_flags"))
+    return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kAlignThreads);
@@ -332,14 +326,9 @@ extern "C" int fus_moe_align_ex(const int* ids, int numel, int E, int block_m, i
   cudaStream_t st = as_stream(stream);
   if (numel <= kAlignSmallMax) {
     const size_t sm = small_smem_bytes(E);
-    static bool attr_done = false;
-    if (!attr_done) {
-      cudaError_t e = cudaFuncSetAttribute(align_small_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)small_smem_bytes(kAlignMaxE));
-      if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "moe_align attr: %s", cudaGetErrorString(e));
-      attr_done = true;
-    }
+    if (int rc = ensure_smem_attr((const void*)align_small_kernel,
+                                   (int)small_smem_bytes(kAlignMaxE), "moe_align"))
+      return rc;
     align_small_kernel<<<1, kAlignThreads, sm, st>>>(ids, numel, E, block_m, sorted_ids, sorted_cap,
                                                     expert_ids, blocks_cap, ntp, pos_of, balanced,
                                                     status);
@@ -353,13 +342,10 @@ extern "C" int fus_moe_align_ex(const int* ids, int numel, int E, int block_m, i
   int* hist = rank + numel;
   int* se = hist + (size_t)nchunks * E;
   const size_t sm = sizeof(int) * ((size_t)kAlignWarps * E + E);
-  static bool attr_done2 = false;
-  if (!attr_done2) {
-    cudaError_t e = cudaFuncSetAttribute(align_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(sizeof(int) * ((size_t)kAlignWarps * kAlignMaxE + kAlignMaxE)));
-    if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "moe_align attr: %s", cudaGetErrorString(e));
-    attr_done2 = true;
-  }
+  if (int rc = ensure_smem_attr((const void*)align_rank_kernel,
+                                 (int)(sizeof(int) * ((size_t)kAlignWarps * kAlignMaxE + kAlignMaxE)),
+                                 "moe_align"))
+    return rc;
   align_rank_kernel<<<nchunks, kAlignThreads, sm, st>>>(ids, numel, E, rank, hist, status);
   align_scan_kernel<<<1, kAlignThreads, 0, st>>>(hist, nchunks, E, block_m, numel, sorted_ids,
                                                  sorted_cap, expert_ids, blocks_cap, ntp, se,

@@ -4,6 +4,8 @@
 #include <stdio.h>
 
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "host_util.h"
 
@@ -30,6 +32,21 @@ int num_sms() {
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
   return n > 0 ? n : 148;
+}
+
+int ensure_smem_attr(const void* fn, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;  // (kernel, device, bytes)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(fn, dev, bytes);
+  if (done.count(key)) return FUS_OK;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "%s attr: %s", what, cudaGetErrorString(e));
+  done.insert(key);
+  return FUS_OK;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,

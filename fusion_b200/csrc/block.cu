@@ -88,6 +88,26 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   return true;
 }
 
+// the shared expert's weight regions the decode front end asks L2 for (none unless
+// FUS_BLOCK_PREFETCH_SHARED is set and the block has a shared expert)
+struct Prefetch {
+  const void* p0 = nullptr;
+  long b0 = 0;
+  const void* p1 = nullptr;
+  long b1 = 0;
+};
+
+Prefetch prefetch_for(const fus_moe_block_desc* d) {
+  Prefetch pf;
+  if (d->w13s && d->w2s && (d->flags & FUS_BLOCK_PREFETCH_SHARED)) {
+    pf.p0 = d->w13s;
+    pf.b0 = 2L * d->I * d->H * 2;
+    pf.p1 = d->w2s;
+    pf.b1 = (long)d->H * d->I * 2;
+  }
+  return pf;
+}
+
 }  // namespace
 
 using namespace fus;
@@ -113,12 +133,9 @@ extern "C" size_t fus_moe_block_workspace(const fus_moe_block_desc* d, int T, in
   return L.total;
 }
 
-extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h, const void* r,
-                                     int T, int block_n, void* out, void* h1, float* topw,
-                                     int* topi, void* workspace, size_t ws_bytes, void* stream,
-                                     int* status) {
-  if (!d || !h || !r || !out || !h1 || !topw || !topi || !workspace)
-    return set_error(FUS_E_INVALID, "moe_block: null argument");
+extern "C" int fus_moe_block_check(const fus_moe_block_desc* d, int T, int block_n,
+                                   size_t ws_bytes) {
+  if (!d) return set_error(FUS_E_INVALID, "moe_block: null argument");
   if (T < 0) return set_error(FUS_E_INVALID, "moe_block: T < 0");
   if (T == 0) return FUS_OK;
   if (!d->gamma || !d->wa || !d->w13 || !d->w2 || (!d->w13s) != (!d->w2s))
@@ -126,7 +143,27 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   if (block_n <= 0) block_n = fus_moe_block_pick_block_n(T, d->E, d->topk);
   BlockLayout L;
   if (!layout_for(d, T, block_n, L)) return set_error(FUS_E_INVALID, "moe_block: bad sizes");
-  if (ws_bytes < L.total) return set_error(FUS_E_INVALID, "moe_block: workspace %zu < %zu", ws_bytes, L.total);
+  if (ws_bytes < L.total)
+    return set_error(FUS_E_INVALID, "moe_block: workspace %zu < %zu", ws_bytes, L.total);
+  if (small_path(d, T)) {
+    const Prefetch pf = prefetch_for(d);
+    return route_small_check(T, d->H, d->E, d->topk, d->n_group, d->topk_group, block_n,
+                             d->nplanes, pf.p0, pf.b0, pf.p1, pf.b1);
+  }
+  return FUS_OK;
+}
+
+extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h, const void* r,
+                                     int T, int block_n, void* out, void* h1, float* topw,
+                                     int* topi, void* workspace, size_t ws_bytes, void* stream,
+                                     int* status) {
+  if (!d || !h || !r || !out || !h1 || !topw || !topi || !workspace)
+    return set_error(FUS_E_INVALID, "moe_block: null argument");
+  if (int rc = fus_moe_block_check(d, T, block_n, ws_bytes)) return rc;
+  if (T == 0) return FUS_OK;
+  if (block_n <= 0) block_n = fus_moe_block_pick_block_n(T, d->E, d->topk);
+  BlockLayout L;
+  layout_for(d, T, block_n, L);
   const int H = d->H, I = d->I, E = d->E, K = d->topk;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   auto at = [&](size_t off) { return base + off; };
@@ -148,16 +185,15 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
 
   int rc;
   const bool small = small_path(d, T);
-  const bool pf_shared = shared && (d->flags & FUS_BLOCK_PREFETCH_SHARED);
   if (small) {
+    const Prefetch pf = prefetch_for(d);
     // decode: norm + router + top-k + layout in one launch; it also clears the merge
     // counters, so the down projection needs no separate reset
     if ((rc = route_small_launch(h, r, d->gamma, d->eps, d->wa, d->nplanes, d->bias, T, H, E, K,
                                  d->routed_scale, d->renorm, d->n_group, d->topk_group, h1, x2,
                                  partial, topw, topi, block_n, sorted, L.cap, eids, L.blocks_cap,
                                  ntp, done, counters, T * L.tiles, stream, status,
-                                 pf_shared ? d->w13s : nullptr, 2L * I * H * 2,
-                                 pf_shared ? d->w2s : nullptr, (long)H * I * 2)))
+                                 pf.p0, pf.b0, pf.p1, pf.b1)))
       return rc;
   } else {
     if ((rc = fus_add_rmsnorm(h, H, r, H, d->gamma, h1, H, x2, H, T, H, d->eps, 1, 1, stream,

@@ -508,14 +508,9 @@ namespace {
 template <int BN, int EPI>
 int launch_p(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t st) {
   using Cfg = PersistCfg<BN>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(grouped_gemm_persistent<BN, EPI>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
-                                                cudaGetErrorString(attr_err));
+  if (int rc = ensure_smem_attr((const void*)grouped_gemm_persistent<BN, EPI>, Cfg::SMEM_BYTES,
+                                 "grouped_gemm_persistent"))
+    return rc;
   grouped_gemm_persistent<BN, EPI><<<grid, kPThreads, Cfg::SMEM_BYTES, st>>>(
       maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[4], maps[5], a);
   return check_launch("grouped_gemm_persistent");
@@ -535,13 +530,13 @@ int launch_persist(int bn, const CUtensorMap* maps, const GemmArgs& a, int grid,
 template <int EPI>
 int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStream_t st) {
   using Cfg = PairCfg<EPI>;
+  if (int rc = ensure_smem_attr((const void*)grouped_gemm_pair<EPI>, Cfg::SMEM_BYTES,
+                                 "grouped_gemm_pair"))
+    return rc;
+  // co-resident cluster count (same on every B200; computed on the first device used)
   static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
   static int max_clusters = 0;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(grouped_gemm_pair<EPI>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-    if (attr_err != cudaSuccess) return;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2));
     cfg.blockDim = dim3(kPThreads);
@@ -552,8 +547,6 @@ int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStre
       max_clusters = 0;
     }
   });
-  if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
-                                                cudaGetErrorString(attr_err));
   // one resident cluster per SM pair; clusters beyond the co-resident count would only
   // queue behind the first wave
   long clusters = max_clusters > 0 ? max_clusters : num_sms() / 2;
@@ -566,14 +559,9 @@ int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStre
 template <int BN, int EPI, int MT>
 int launch_t(const CUtensorMap* maps, const GemmArgs& a, int grid, cudaStream_t st) {
   using Cfg = GemmCfg<BN, MT>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, MT>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess) return set_error(FUS_E_LAUNCH, "cudaFuncSetAttribute: %s",
-                                                cudaGetErrorString(attr_err));
+  if (int rc = ensure_smem_attr((const void*)grouped_gemm_kernel<BN, EPI, MT>, Cfg::SMEM_BYTES,
+                                 "grouped_gemm"))
+    return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

@@ -23,6 +23,10 @@ int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t
 int make_tmap_store_2d(CUtensorMap* m, const void* base, bool f32, uint64_t inner, uint64_t rows,
                        uint64_t ld, uint32_t box_inner, uint32_t box_rows);
 int num_sms();
+// Raises `fn`'s dynamic shared-memory limit to `bytes` on the current device, once per
+// (kernel, device): the attribute is per device, so a process that drives several GPUs
+// sets it on each. Thread-safe. Returns FUS_OK or FUS_E_LAUNCH with the CUDA error text.
+int ensure_smem_attr(const void* fn, int bytes, const char* what);
 
 // Grouped GEMM entry used inside the library with programmatic dependent launch:
 // pdl = 0 plain launch; 1 launched early, every thread waits for the predecessor before
@@ -59,6 +63,12 @@ int route_small_launch(const void* h, const void* r, const void* gamma, float ep
                        int* expert_ids, int blocks_cap, int* ntp, int* done, int* zero,
                        int zero_n, void* stream, int* status, const void* pf0 = nullptr,
                        long pf0_bytes = 0, const void* pf1 = nullptr, long pf1_bytes = 0);
+
+// route_small_launch's shape and prefetch-region checks, without pointers to device data
+// (host only: fus_moe_block_check runs it on the CPU with the block's own arguments)
+int route_small_check(int T, int H, int E, int topk, int n_group, int topk_group, int block_m,
+                      int nplanes, const void* pf0, long pf0_bytes, const void* pf1,
+                      long pf1_bytes);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -342,6 +342,29 @@ __global__ void __launch_bounds__(kRouteThreads)
 using namespace fus;
 
 namespace fus {
+int route_small_check(int T, int H, int E, int topk, int n_group, int topk_group, int block_m,
+                      int nplanes, const void* pf0, long pf0_bytes, const void* pf1,
+                      long pf1_bytes) {
+  if (n_group < 1) n_group = 1;
+  if (topk_group < 1) topk_group = 1;
+  if ((pf0_bytes > 0 && (!pf0 || pf0_bytes % 16 || !aligned16(pf0))) ||
+      (pf1_bytes > 0 && (!pf1 || pf1_bytes % 16 || !aligned16(pf1))))
+    return set_error(FUS_E_INVALID, "route_small: prefetch regions must be 16-byte granular");
+  if (n_group > 1 && (E % n_group || (E / n_group) % 8 ||
+                      ((E / n_group / 8) & (E / n_group / 8 - 1)) || n_group > 32 ||
+                      topk_group > n_group || topk > topk_group * (E / n_group)))
+    return set_error(FUS_E_UNSUPPORTED, "route_small: n_group=%d topk_group=%d E=%d", n_group,
+                     topk_group, E);
+  if (T < 1 || T > kRouteMaxT || E < 2 || E > 256 || E % 2 || topk < 1 || topk > 16 ||
+      topk > E || T * topk > 256 || H % 8 || H <= 0 || H > 8192 || block_m < 1 ||
+      (nplanes != 1 && nplanes != 3))
+    return set_error(FUS_E_UNSUPPORTED, "route_small: T=%d E=%d topk=%d H=%d unsupported", T, E,
+                     topk, H);
+  const size_t smem = (size_t)T * H * 2;
+  if (smem > 200 * 1024) return set_error(FUS_E_UNSUPPORTED, "route_small: T*H too large");
+  return FUS_OK;
+}
+
 int route_small_launch(const void* h, const void* r, const void* gamma, float eps, const void* wa,
                        int nplanes, const float* bias, int T, int H, int E, int topk, float scale,
                        int renorm, int n_group, int topk_group, void* h1, void* x2, float* logits,
@@ -349,37 +372,22 @@ int route_small_launch(const void* h, const void* r, const void* gamma, float ep
                        int* expert_ids, int blocks_cap, int* ntp, int* done, int* zero,
                        int zero_n, void* stream, int* status, const void* pf0, long pf0_bytes,
                        const void* pf1, long pf1_bytes) {
+  if (int rc = route_small_check(T, H, E, topk, n_group, topk_group, block_m, nplanes, pf0,
+                                 pf0_bytes, pf1, pf1_bytes))
+    return rc;
   if (n_group < 1) n_group = 1;
-  if ((pf0_bytes > 0 && (!pf0 || pf0_bytes % 16 || !aligned16(pf0))) ||
-      (pf1_bytes > 0 && (!pf1 || pf1_bytes % 16 || !aligned16(pf1))))
-    return set_error(FUS_E_INVALID, "route_small: prefetch regions must be 16-byte granular");
   if (topk_group < 1) topk_group = 1;
-  if (n_group > 1 && (E % n_group || (E / n_group) % 8 ||
-                      ((E / n_group / 8) & (E / n_group / 8 - 1)) || n_group > 32 ||
-                      topk_group > n_group || topk > topk_group * (E / n_group)))
-    return set_error(FUS_E_UNSUPPORTED, "route_small: n_group=%d topk_group=%d E=%d", n_group,
-                     topk_group, E);
   if (!h || !r || !gamma || !wa || !h1 || !x2 || !logits || !topw || !topi || !sorted_ids ||
       !expert_ids || !ntp || !done || (zero_n > 0 && !zero))
     return set_error(FUS_E_INVALID, "route_small: null argument");
-  if (T < 1 || T > kRouteMaxT || E < 2 || E > 256 || E % 2 || topk < 1 || topk > 16 ||
-      topk > E || T * topk > 256 || H % 8 || H <= 0 || H > 8192 || block_m < 1 ||
-      (nplanes != 1 && nplanes != 3))
-    return set_error(FUS_E_UNSUPPORTED, "route_small: T=%d E=%d topk=%d H=%d unsupported", T, E,
-                     topk, H);
   if (!aligned16(h) || !aligned16(r) || !aligned16(gamma) || !aligned16(wa) || !aligned16(h1) ||
       !aligned16(x2))
     return set_error(FUS_E_INVALID, "route_small: rows must be 16-byte aligned");
   const size_t smem = (size_t)T * H * 2;
   const size_t smem_min = sizeof(int) * (kRouteMaxT * 16 + 3 * 256);
   const size_t dyn = smem > smem_min ? smem : smem_min;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(route_small_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return set_error(FUS_E_LAUNCH, "route_small attr: %s", cudaGetErrorString(e));
-    attr = true;
-  }
+  if (int rc = ensure_smem_attr((const void*)route_small_kernel, 200 * 1024, "route_small"))
+    return rc;
   if (dyn > 200 * 1024) return set_error(FUS_E_UNSUPPORTED, "route_small: T*H too large");
   RouteArgs a{};
   a.h = (const __nv_bfloat16*)h;

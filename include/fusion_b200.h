@@ -393,6 +393,10 @@ typedef struct fus_moe_block_desc {
 
 int fus_moe_block_pick_block_n(int T, int E, int topk);
 size_t fus_moe_block_workspace(const fus_moe_block_desc* d, int T, int block_n);
+/* Every argument check fus_moe_block_forward makes before its first launch, on the host
+ * only (no device access; weight pointers are only compared with NULL and 16-byte
+ * alignment): FUS_OK exactly when forward would reach its kernels with these sizes. */
+int fus_moe_block_check(const fus_moe_block_desc* d, int T, int block_n, size_t ws_bytes);
 int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h, const void* r, int T,
                           int block_n, void* out, void* h1, float* topw, int* topi,
                           void* workspace, size_t ws_bytes, void* stream, int* status);

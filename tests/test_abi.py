@@ -68,6 +68,51 @@ def test_block_workspace_grows_with_T():
         prev = ws
 
 
+def _glm_desc(shared: bool, flags: int) -> L.BlockDesc:
+    """A GLM-5.2 block descriptor with fake, 256-byte aligned weight addresses (host
+    checks compare pointers with NULL and test alignment only; nothing is dereferenced)."""
+    d = L.BlockDesc(H=6144, I=2048, E=256, topk=8, eps=1e-5, routed_scale=2.5, renorm=1,
+                    nplanes=3, n_group=1, topk_group=1, flags=flags)
+    for i, name in enumerate(("gamma", "wa", "w13", "w2")):
+        setattr(d, name, ctypes.c_void_p(0x10000 * (i + 1)))
+    d.bias = ctypes.c_void_p(0x90000)
+    if shared:
+        d.w13s = ctypes.c_void_p(0xA0000)
+        d.w2s = ctypes.c_void_p(0xB0000)
+    return d
+
+
+def test_block_check_accepts_default_calls_at_every_size():
+    """The block's pre-launch checks pass for the default descriptor (prefetch off) at
+    decode and prefill sizes, with and without the shared expert: a decode call whose
+    front end would reject its own arguments fails here, on the CPU."""
+    lib = L.lib()
+    for shared in (True, False):
+        for flags in (0, L.FUS_BLOCK_PREFETCH_SHARED):
+            d = _glm_desc(shared, flags)
+            for T in (1, 2, 8, 16, 17, 32, 256, 2048, 8192):
+                bn = lib.fus_moe_block_pick_block_n(T, 256, 8)
+                ws = lib.fus_moe_block_workspace(ctypes.byref(d), T, bn)
+                rc = lib.fus_moe_block_check(ctypes.byref(d), T, 0, ws)
+                assert rc == 0, (shared, flags, T, L.last_error())
+
+
+def test_block_check_rejects_bad_arguments():
+    lib = L.lib()
+    d = _glm_desc(True, 0)
+    ws = lib.fus_moe_block_workspace(ctypes.byref(d), 1, 0)
+    assert lib.fus_moe_block_check(ctypes.byref(d), 1, 0, ws - 1) == -1
+    assert "workspace" in L.last_error()
+    d.w2s = None  # shared gate-up without shared down
+    assert lib.fus_moe_block_check(ctypes.byref(d), 1, 0, ws) == -1
+    assert "missing weights" in L.last_error()
+    d = _glm_desc(True, L.FUS_BLOCK_PREFETCH_SHARED)
+    d.w13s = ctypes.c_void_p(0xA0008)  # prefetch region not 16-byte aligned
+    assert lib.fus_moe_block_check(ctypes.byref(d), 1, 0, ws) == -1
+    assert "16-byte" in L.last_error()
+    assert lib.fus_moe_block_check(ctypes.byref(_glm_desc(True, 0)), 0, 0, 0) == 0
+
+
 def test_synth_host_deterministic_and_sliceable():
     a = synth.make("w13", (4, 64, 96), 5)
     b = synth.make("w13", (4, 64, 96), 5)

@@ -163,7 +163,7 @@ SIGNATURES: dict[str, tuple] = {
     "fus_ep_plan_dedup": (i32, [vp, i32, i32, i32, i32, vp, vp, vp, vp]),
     "fus_ep_pack_dedup": (i32, [vp, i64, i32, vp, i32, i32, vp, vp, i32, i32, vp, vp, vp, i64,
                                 vp, vp, vp, vp, i32, vp, vp]),
-    "fus_ep_return_rowmap": (i32, [vp, i32, vp, i32, i32, vp, vp, i32, vp, vp, vp]),
+    "fus_ep_return_rowmap": (i32, [vp, i32, vp, vp, i32, i32, vp, vp, i32, vp, vp, vp]),
     "fus_ep_partial_sum": (i32, [vp, i64, i32, vp, vp, i32, i32, vp, i64, vp, vp]),
     "fus_ipc_handle": (i32, [vp, vp, C.POINTER(C.c_size_t)]),
     "fus_ipc_open": (i32, [vp, sz, C.POINTER(C.c_void_p)]),

@@ -186,15 +186,26 @@ __global__ void ep_pack_dedup_kernel(const __nv_bfloat16* __restrict__ x, long l
 // the return buffer. Entry x of the dispatch layout holds flat slot f = i*K + j of
 // received row i; row i came from source s (row_prefix[s] <= i < row_prefix[s + 1]) and
 // its row goes to pair_prefix[s] + ret_idx[f]. Pads (f >= n*K) stay past every row.
+// Only the first *ntp entries (the padded total) of the layout are written by moe_align;
+// entries past it are not read and map to the pad row n*K.
 __global__ void ep_return_rowmap_kernel(const int* __restrict__ sorted_ids, int cap,
+                                        const int* __restrict__ ntp,
                                         const int* __restrict__ ret_idx, int K, int nK,
                                         const int* __restrict__ row_prefix,
                                         const int* __restrict__ pair_prefix, int W,
                                         int* __restrict__ rowmap, int* status) {
+  const int used = ntp ? min(cap, __ldg(ntp)) : cap;
   for (int x = blockIdx.x * blockDim.x + threadIdx.x; x < cap; x += gridDim.x * blockDim.x) {
+    if (x >= used) {
+      rowmap[x] = nK;
+      continue;
+    }
     const int f = __ldg(sorted_ids + x);
     int out = f < nK ? -1 : f;
-    if (f < nK) {
+    if (f < 0) {
+      raise_status(status, FUS_ERR_CAPACITY);
+      out = nK;
+    } else if (f < nK) {
       const int i = f / K;
       int s = 0;
       while (s + 1 < W && __ldg(row_prefix + s + 1) <= i) ++s;
@@ -323,7 +334,8 @@ extern "C" int fus_ep_pack_dedup(const void* x, long ldx, int H, const int* send
   return check_launch("ep_pack_dedup");
 }
 
-extern "C" int fus_ep_return_rowmap(const int* sorted_ids, int cap, const int* ret_idx, int n,
+extern "C" int fus_ep_return_rowmap(const int* sorted_ids, int cap, const int* ntp,
+                                    const int* ret_idx, int n,
                                     int K, const int* row_prefix, const int* pair_prefix, int W,
                                     int* rowmap, void* stream, int* status) {
   if (!sorted_ids || !ret_idx || !row_prefix || !pair_prefix || !rowmap || cap < 0 || n < 0 ||
@@ -333,7 +345,7 @@ extern "C" int fus_ep_return_rowmap(const int* sorted_ids, int cap, const int* r
   int grid = ceil_div(cap, 256);
   if (grid > 4 * num_sms()) grid = 4 * num_sms();
   ep_return_rowmap_kernel<<<grid, 256, 0, as_stream(stream)>>>(
-      sorted_ids, cap, ret_idx, K, n * K, row_prefix, pair_prefix, W, rowmap, status);
+      sorted_ids, cap, ntp, ret_idx, K, n * K, row_prefix, pair_prefix, W, rowmap, status);
   return check_launch("ep_return_rowmap");
 }
 

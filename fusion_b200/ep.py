@@ -534,7 +534,7 @@ class CudaEPBackend:
             return torch.tensor(out, dtype=torch.int32, device=self.dev)
         rowmap = torch.empty_like(L["sorted_ids"])
         ops.ep_return_rowmap(L["sorted_ids"], ret_idx, leid.shape[1], prefix(rows_in),
-                             prefix(pairs_in), rowmap)
+                             prefix(pairs_in), rowmap, ntp=L["ntp"])
         g2 = ops.gemm_group(self.w2, L["act"], y, expert_ids=L["eids"], ntp=L["ntp"],
                             max_blocks=L["maxb"], row_map=rowmap, row_limit=P, flags=L["ws"],
                             live_ids=L["sorted_ids"], live_limit=L["R"])

@@ -371,11 +371,12 @@ def ep_pack_dedup(x, send_ids, n: int, W: int, topi, topw, E_loc: int, rows, lei
            _p(ret_out), _p(w_out), _p(pos), zero_row, _stream(), _sp())
 
 
-def ep_return_rowmap(sorted_ids, ret_idx, K: int, row_prefix, pair_prefix, rowmap):
-    """Owner's w2 row map into the return buffer (see fus_ep_return_rowmap)."""
+def ep_return_rowmap(sorted_ids, ret_idx, K: int, row_prefix, pair_prefix, rowmap, ntp=None):
+    """Owner's w2 row map into the return buffer (see fus_ep_return_rowmap); ``ntp``: the
+    layout's padded total (entries of sorted_ids past it are not read)."""
     n = ret_idx.numel() // K
     W = row_prefix.numel() - 1
-    L.call("fus_ep_return_rowmap", _p(sorted_ids), sorted_ids.numel(), _p(ret_idx), n, K,
+    L.call("fus_ep_return_rowmap", _p(sorted_ids), sorted_ids.numel(), _p(ntp), _p(ret_idx), n, K,
            _p(row_prefix), _p(pair_prefix), W, _p(rowmap), _stream(), _sp())
 
 

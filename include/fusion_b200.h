@@ -444,6 +444,8 @@ int fus_ep_unpack(const void* rows, long ldr, int H, const int* send_ids, int n,
  *                     slot f = sorted_ids[x] < n*K of row i = f / K from source s
  *                     (row_prefix[s] <= i < row_prefix[s+1]) -> pair_prefix[s] +
  *                     ret_idx[f]; pads stay >= n*K. row_prefix / pair_prefix: W+1 ints.
+ *                     ntp: the layout's padded total (moe_align's ntp; entries from it on
+ *                     are never read and map to n*K) or NULL when all cap entries are set.
  * fus_ep_partial_sum: owner side, out[i] = bf16(sum_{j: leid[i*K+j] >= 0} w[i*K+j] *
  *                     y[i*K+j]) in fp32, slot order (y: expert rows in slot order).
  * Pair combine (exact): the owner returns one expert row per pair, the source merges
@@ -457,7 +459,8 @@ int fus_ep_pack_dedup(const void* x, long ldx, int H, const int* send_ids, int n
                       const int* topi, const float* topw, int K, int E_loc, const int* pair_pos,
                       const int* counts, void* rows, long ldr, int* leid_out, int* ret_out,
                       float* w_out, int* pos, int zero_row, void* stream, int* status);
-int fus_ep_return_rowmap(const int* sorted_ids, int cap, const int* ret_idx, int n, int K,
+int fus_ep_return_rowmap(const int* sorted_ids, int cap, const int* ntp, const int* ret_idx,
+                         int n, int K,
                          const int* row_prefix, const int* pair_prefix, int W, int* rowmap,
                          void* stream, int* status);
 int fus_ep_partial_sum(const void* y, long ldy, int H, const int* leid, const float* w, int n,

@@ -163,6 +163,15 @@ def test_ep_dedup_plan_pack_partial_kernels():
         ref_map.append(int([0, pairs_in[0], pairs_in[0]][src] + ret_src.reshape(-1)[f]))
     assert np.array_equal(rowmap.cpu().numpy(), np.array(ref_map))
     assert ops.read_status() == 0
+    # a layout buffer longer than its padded total: the tail is never written by
+    # moe_align (junk here, negative and in-range values) and must not be read
+    junk = np.concatenate([sorted_ids, np.array([-7, 3, 1 << 30, 0], np.int32)])
+    ntp = torch.tensor([sorted_ids.size], dtype=torch.int32, device=DEV)
+    rowmap2 = torch.empty(junk.size, dtype=torch.int32, device=DEV)
+    ops.ep_return_rowmap(torch.from_numpy(junk).to(DEV), torch.from_numpy(ret_src).to(DEV), K,
+                         rp, pp, rowmap2, ntp=ntp)
+    finish()
+    assert np.array_equal(rowmap2.cpu().numpy(), np.array(ref_map + [n * K] * 4))
     # owner: partial = bf16(sum over its slots of w * y); hole rows hold NaN and must be
     # skipped, not multiplied by a zero weight
     y = torch.randn(n * K, H, device=DEV).to(torch.bfloat16)
@@ -301,8 +310,12 @@ def _two_rank_worker(rank, port, q):
                            w["w2s"], E=D.E, rank=rank)
         ep = ExpertParallelMoE(be)
         h, r = synth.make_inputs(70 + rank, 24, D, "cuda")
-        out = ep(h, r)["out"]
+        out = ep(h, r, dispatch="pairs")["out"]
         stage("prefill step (all_to_all) done")
+        out_dd = ep(h, r, dispatch="dedup")["out"]
+        torch.cuda.synchronize()
+        ops.check_status()
+        stage("prefill step (deduplicated dispatch) done")
         h2, r2 = synth.make_inputs(90 + rank, 2, D, "cuda")
         g = EPDecodeGraph(ep, 2, D.H, "cuda", exchange="nccl")  # all_to_all in a CUDA graph
         g.h.copy_(h2)
@@ -324,7 +337,8 @@ def _two_rank_worker(rank, port, q):
         torch.cuda.synchronize()
         ops.check_status()
         same = bool(torch.equal(out2.view(torch.int16), out3.view(torch.int16)) and
-                    torch.equal(out2.view(torch.int16), out4.view(torch.int16)))
+                    torch.equal(out2.view(torch.int16), out4.view(torch.int16)) and
+                    torch.equal(out.view(torch.int16), out_dd.view(torch.int16)))
         q.put((rank, (out.float().cpu().numpy(), out2.float().cpu().numpy(), same)))
         stage("results sent")
         del g  # the graph holds NCCL work: release it before the communicator
@@ -332,6 +346,11 @@ def _two_rank_worker(rank, port, q):
         gp.close()
         st.close()
         dist.barrier()
+    except BaseException as e:  # noqa: BLE001 - report, so the parent does not wait out its timeout
+        import traceback
+
+        q.put((rank, f"rank {rank} failed: {e!r}\n{traceback.format_exc()}"))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -350,7 +369,13 @@ def test_ep_two_nccl_ranks_match_block():
         p.start()
     # drain before joining: a child cannot exit while its result is still in the pipe
     try:
-        outs = dict(q.get(timeout=240) for _ in range(2))
+        outs = {}
+        while len(outs) < 2:
+            rank, res = q.get(timeout=240)
+            # a rank that fails posts its traceback at once (its peer may be stuck in a
+            # collective until the process-group timeout)
+            assert not isinstance(res, str), res
+            outs[rank] = res
         for p in ps:
             p.join(timeout=60)
     finally:
@@ -361,7 +386,8 @@ def test_ep_two_nccl_ranks_match_block():
     w = synth.make_block_weights(404, D, DEV)
     blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"])
     for rank in range(2):
-        assert outs[rank][2], "NVLink exchange differs from the all_to_all exchange"
+        assert outs[rank][2], ("NVLink exchange differs from the all_to_all exchange, or "
+                               "the deduplicated dispatch from the per-pair one")
         for (seed, T), got in zip(((70, 24), (90, 2)), outs[rank][:2]):
             h, r = synth.make_inputs(seed + rank, T, D, DEV)
             ref = blk(h, r)

@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--impl", choices=["fusion", "reference"], default="fusion")
     ap.add_argument("--regimes", default=",".join(REGIMES),
                     help="extra T values measured besides the headline ('' for none)")
+    ap.add_argument("--strong", default="256,2048,8192,8192z",
+                    help="N>1: global batch sizes split over the ranks (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefetch-shared", action="store_true",
                     help="decode: the front end pulls the shared expert's weights into L2")
@@ -62,30 +64,41 @@ def parse():
 # -------------------------------------------------------------------------------------
 # CPU side: the reference path restated (oracle), timed on the host cores
 # -------------------------------------------------------------------------------------
-def cpu_reference(T: int, steps: int, warmup: int, budget_s: float = 60.0) -> dict:
+H, I, E, TOPK = 6144, 2048, 256, 8  # GLM-5.2 block dims (fusion_b200/config.py)
+
+
+def cpu_reference(T: int, steps: int, warmup: int, budget_s: float = 60.0,
+                  ranks: int = 1) -> dict:
+    """The reference path on the host cores: ``ranks`` ranks' worth of T tokens each (the
+    GPU arm's inputs: rank g's tokens are seed SEED*1000 + T + g), every step one block
+    over all of them. Inputs come from the numpy restatement of the generator, so this
+    arm loads no part of the CUDA library."""
     import numpy as np
-    import torch
+    from threadpoolctl import threadpool_limits
 
-    from fusion_b200 import synth
     from oracle import reference_np as O
+    from oracle import synth_np as S
 
-    d = synth.Dims()
-    h = synth.make("h", (T, d.H), SEED * 1000 + T).float().numpy()
-    r = synth.make("r", (T, d.H), SEED * 1000 + T).float().numpy()
-    gamma = synth.make("gamma", (d.H,), SEED).float().numpy()
-    gw = synth.make("gate_w", (d.E, d.H), SEED).numpy()
-    bias = synth.make("bias", (d.E,), SEED).numpy()
+    cores = os.cpu_count() or 1
+    # torchrun exports OMP_NUM_THREADS=1; the reference arm uses every host core
+    threadpool_limits(cores)
+    h = np.concatenate([S.make("h", (T, H), SEED * 1000 + T + g) for g in range(ranks)])
+    r = np.concatenate([S.make("r", (T, H), SEED * 1000 + T + g) for g in range(ranks)])
+    gamma = S.make("gamma", (H,), SEED)
+    gw = S.make("gate_w", (E, H), SEED)
+    bias = S.make("bias", (E,), SEED)
     x2, _ = O.add_rmsnorm(h, r, gamma)
     _, _, ids = O.router(x2, gw, bias)
     used = sorted(set(ids.flatten().tolist()))
     # weights resident in host memory before timing, as they are in HBM on the GPU side
-    w13 = {e: synth.expert_weight("w13", e, d, SEED).float().numpy() for e in used}
-    w2 = {e: synth.expert_weight("w2", e, d, SEED).float().numpy() for e in used}
-    w13s = synth.make("w13s", (2 * d.I, d.H), SEED).float().numpy()
-    w2s = synth.make("w2s", (d.H, d.I), SEED).float().numpy()
+    w13 = {e: S.expert_weight("w13", e, H, I, SEED) for e in used}
+    w2 = {e: S.expert_weight("w2", e, H, I, SEED) for e in used}
+    w13s = S.make("w13s", (2 * I, H), SEED)
+    w2s = S.make("w2s", (H, I), SEED)
+    T = T * ranks
 
     def step():
-        O.moe_block(h, r, gamma, gw, bias, w13.__getitem__, w2.__getitem__, w13s, w2s, d.E)
+        O.moe_block(h, r, gamma, gw, bias, w13.__getitem__, w2.__getitem__, w13s, w2s, E)
 
     for _ in range(max(1, min(warmup, 2))):
         step()
@@ -98,11 +111,10 @@ def cpu_reference(T: int, steps: int, warmup: int, budget_s: float = 60.0) -> di
         if time.perf_counter() > t_end:
             break
     per = statistics.fmean(times)
-    threads = int(os.environ.get("OMP_NUM_THREADS", 0)) or (os.cpu_count() or 1)
     return {
         "value": T / per,
         "unit": UNIT,
-        "cores": threads,
+        "cores": cores,
         "kind": "port",
         "ms_per_step": per * 1e3,
         "steps_timed": len(times),
@@ -111,17 +123,31 @@ def cpu_reference(T: int, steps: int, warmup: int, budget_s: float = 60.0) -> di
     }
 
 
+def headline_config(world: int) -> dict:
+    """The workload both arms report (identical dicts: same tokens, same block)."""
+    if world == 1:
+        wl = f"decode_T{HEADLINE_T} (BASELINE config 1): full GLM-5.2 MoE block, 256 experts top-8 + shared"
+    else:
+        wl = (f"decode_T{HEADLINE_T} per rank x {world} ranks (BASELINE config 1): full GLM-5.2 "
+              f"MoE block over {world * HEADLINE_T} tokens, 256 experts top-8 + shared")
+    return {"workload": wl, "T": HEADLINE_T * world, "T_per_rank": HEADLINE_T, "H": H, "I": I,
+            "E": E, "topk": TOPK, "n_ranks": world,
+            "l2": "flushed by a 512 MB write before every timed step",
+            "parallelism": "single" if world == 1 else f"ep{world}"}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    res = cpu_reference(HEADLINE_T, args.steps, args.warmup)
+    res = cpu_reference(HEADLINE_T, args.steps, args.warmup, ranks=world)
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": res["value"],
         "unit": UNIT,
-        "n_gpus": args.gpus,
+        "n_gpus": world,
         "steps": res["steps_timed"],
         "warmup": args.warmup,
         "ms_per_step": res["ms_per_step"],
@@ -130,8 +156,7 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded, bit-identical to the GPU arm's inputs)",
-        "config": {"workload": f"decode_T{HEADLINE_T} (BASELINE config 1)", "T": HEADLINE_T,
-                   "H": 6144, "I": 2048, "E": 256, "topk": 8},
+        "config": headline_config(world),
         "cpu_baseline": res,
         "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -202,12 +227,15 @@ class ClockSampler:
 # -------------------------------------------------------------------------------------
 def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
            stdout_fd: int) -> None:
-    """N > 1: expert parallelism over NCCL (fusion_b200.ep). Rank g holds experts
-    [32g, 32g+32) at 8 GPUs; every rank routes its own T tokens (weak scaling)."""
+    """N > 1: expert parallelism (fusion_b200.ep). Rank g holds experts [gE/N, (g+1)E/N)
+    (32 per GPU at 8 GPUs). The headline and the "_per_rank" regimes are weak scaling
+    (every rank routes its own T tokens); the "_global" regimes are strong scaling (a
+    global batch of T tokens split evenly over the ranks)."""
     import torch
     import torch.distributed as dist
 
     from fusion_b200 import ops, synth, traffic
+    from fusion_b200.block import MoEBlock
     from fusion_b200.ep import (CudaEPBackend, EPDecodeGraph, EPDecodeStep, ExpertParallelMoE,
                                 shard_weights)
 
@@ -216,6 +244,10 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
     be = CudaEPBackend(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"],
                        w["w2s"], E=dims.E, rank=rank)
     ep = ExpertParallelMoE(be)
+    zb = synth.zipf_bias("cuda")
+    be_z = CudaEPBackend(w["gamma"], w["gate_w"], zb, w["w13"], w["w2"], w["w13s"], w["w2s"],
+                         E=dims.E, rank=rank)
+    ep_z = ExpertParallelMoE(be_z)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     pk = traffic.peaks()
 
@@ -226,18 +258,61 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
             return EPDecodeStep(be, T).capture()
         return EPDecodeGraph(ep, T, dims.H, "cuda", exchange="nccl")
 
-    def measure(T: int, steps: int, warmup: int) -> dict:
+    def inputs(T: int, tag: int = 0):
+        return synth.make_inputs(SEED * 1000 + T + rank + tag, T, dims, "cuda")
+
+    # ---- parity: every rank's EP output against the single-GPU block on its tokens ----
+    def parity() -> dict:
+        full = synth.make_block_weights(SEED, dims, "cuda")
+        res = {}
+        for name, T, zipf in (("decode_T1", HEADLINE_T, False), ("prefill_T256", 256, False),
+                              ("prefill_T2048_zipf", 2048, True)):
+            blk = MoEBlock(full["gamma"], full["gate_w"], zb if zipf else full["bias"],
+                           full["w13"], full["w2"], full["w13s"], full["w2s"])
+            h, r = inputs(T)
+            ref = blk(h, r)
+            if T <= 16:
+                g = decode_step(T)
+                g.h.copy_(h)
+                g.r.copy_(r)
+                out = g.replay().clone()
+                topi = (g.topi if isinstance(g, EPDecodeStep) else g.res["topi"]).clone()
+                torch.cuda.synchronize()
+                g.close()
+            else:
+                o = (ep_z if zipf else ep)(h, r)
+                out, topi = o["out"], o["topi"]
+            torch.cuda.synchronize()
+            ops.check_status()
+            rf = ref.out.float()
+            err = float((out.float() - rf).abs().max())
+            rms = float(rf.pow(2).mean().sqrt())
+            ok = torch.tensor([int(err <= 2e-2 * rms and torch.equal(topi, ref.topi))],
+                              device="cuda")
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            e = torch.tensor([err / rms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(e, op=dist.ReduceOp.MAX)
+            res[name] = {"ok": bool(ok.item()), "max_abs_over_rms": float(e.item())}
+        del full
+        torch.cuda.empty_cache()
+        barrier()
+        return res
+
+    par = parity()
+
+    def measure(T: int, steps: int, warmup: int, zipf: bool = False) -> dict:
         if rank == 0:
-            print(f"[bench ep{world}] T={T}/rank", file=sys.stderr, flush=True)
-        h, r = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cuda")
-        small = T <= 16
+            print(f"[bench ep{world}] T={T}/rank zipf={zipf}", file=sys.stderr, flush=True)
+        h, r = inputs(T)
+        small = T <= 16 and not zipf
         if small:  # fixed-slot exchange recorded in a CUDA graph (no host sync)
             g = decode_step(T)
             g.h.copy_(h)
             g.r.copy_(r)
             run = g.replay
         else:
-            run = lambda: ep(h, r)
+            e_ = ep_z if zipf else ep
+            run = lambda: e_(h, r)  # noqa: E731
         for _ in range(warmup):
             flush.zero_()
             run()
@@ -253,7 +328,7 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
             b.record()
             b.synchronize()
             ms.append(a.elapsed_time(b))
-        res = ({"topi": g.topi} if isinstance(g, EPDecodeStep) else g.res) if small else ep(h, r)
+        res = ({"topi": g.topi} if isinstance(g, EPDecodeStep) else g.res) if small else run()
         torch.cuda.synchronize()
         ops.check_status()
         if small:
@@ -268,27 +343,33 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
         ks = traffic.block_kernels(world * T, ne, dims.H, dims.I, dims.E, dims.topk)
         t_roof = traffic.chain_time_s(ks, pk) / world  # the job's work spread over W GPUs
         f, byts = traffic.totals(ks)
-        return {"T_per_rank": T, "ms_per_step": ms_step, "us_per_block": ms_step * 1e3,
-                "tokens_per_s": world * T / (ms_step / 1e3), "distinct_experts": ne,
-                "roofline_us": t_roof * 1e6, "roofline_frac": t_roof / (ms_step / 1e3),
+        return {"T_per_rank": T, "T_global": world * T, "ms_per_step": ms_step,
+                "us_per_block": ms_step * 1e3, "tokens_per_s": world * T / (ms_step / 1e3),
+                "distinct_experts": ne, "roofline_us": t_roof * 1e6,
+                "roofline_frac": t_roof / (ms_step / 1e3),
                 "algorithmic_GB_per_gpu": byts / world / 1e9}
 
     with ClockSampler(local) as clk:
         head = measure(HEADLINE_T, args.steps, max(args.warmup, 3))
         regimes = {}
         for x in [x.strip() for x in args.regimes.split(",") if x.strip()]:
-            if x.endswith("z"):
-                continue  # the skewed-routing regime is measured on one GPU
-            T = int(x)
-            regimes[f"T{T}_per_rank"] = measure(T, max(5, min(args.steps, 20)), 3)
+            zipf = x.endswith("z")
+            T = int(x.rstrip("z"))
+            key = f"T{T}_per_rank" + ("_zipf1.1" if zipf else "")
+            regimes[key] = measure(T, max(5, min(args.steps, 20)), 3, zipf)
+        for x in [x.strip() for x in args.strong.split(",") if x.strip()]:
+            zipf = x.endswith("z")
+            G = int(x.rstrip("z"))
+            if G % world:
+                continue
+            key = f"T{G}_global" + ("_zipf1.1" if zipf else "")
+            regimes[key] = measure(G // world, max(5, min(args.steps, 20)), 3, zipf)
 
     # e2e: pinned host inputs in, output out, every step
     T = HEADLINE_T
     hh, rh = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cpu")
     hh, rh = hh.pin_memory(), rh.pin_memory()
     out_h = torch.empty(T, dims.H, dtype=torch.bfloat16).pin_memory()
-    hd = torch.empty(T, dims.H, dtype=torch.bfloat16, device="cuda")
-    rd = torch.empty_like(hd)
     evs = []
     barrier()
     ge = decode_step(T)
@@ -316,15 +397,13 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
             "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded Irwin-Hall normals, GLM-5.2 shapes, random-init weights)",
-            "config": {"workload": f"decode_T{HEADLINE_T} per rank (BASELINE config 1), "
-                                   f"expert parallel over {world} GPUs",
-                       "T_per_rank": HEADLINE_T, "H": dims.H, "I": dims.I, "E": dims.E,
-                       "topk": dims.topk, "experts_per_gpu": dims.E // world,
-                       "l2": "flushed by a 512 MB write before every timed step",
-                       "parallelism": f"ep{world}",
-                       "timing": f"T<=16: fixed-slot EP step ({exch}) replayed from a "
-                                 "CUDA graph; larger T: eager EP step (NCCL all_to_all); "
-                                 "CUDA events"},
+            "config": headline_config(world),
+            "details": {"experts_per_gpu": dims.E // world,
+                        "timing": f"T<=16: fixed-slot EP step ({exch}) replayed from a "
+                                  "CUDA graph; larger T: eager EP step (NCCL all_to_all, "
+                                  "deduplicated dispatch); CUDA events, max over ranks"},
+            "parity": par,
+            "parity_ok": all(v["ok"] for v in par.values()),
             "us_per_block": head["us_per_block"],
             "roofline": {"kernel": "whole EP block step (per GPU)", "bound": "hbm",
                          "achieved": head["algorithmic_GB_per_gpu"] / (head["ms_per_step"] / 1e3),
@@ -561,15 +640,11 @@ def main() -> None:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded Irwin-Hall normals, GLM-5.2 shapes, random-init weights)",
-            "config": {"workload": f"decode_T{HEADLINE_T} (BASELINE config 1): full GLM-5.2 "
-                                   "MoE block, 256 experts top-8 + shared",
-                       "T": HEADLINE_T, "H": dims.H, "I": dims.I, "E": dims.E,
-                       "topk": dims.topk, "block_n": head["block_n"],
-                       "l2": "flushed by a 512 MB write before every timed step",
-                       "parallelism": "single",
-                       "prefetch_shared": bool(args.prefetch_shared),
-                       "timing": f"CUDA-graph replay of the {launches_per_step(HEADLINE_T)}"
-                                 "-launch block, CUDA events"},
+            "config": headline_config(1),
+            "details": {"block_n": head["block_n"],
+                        "prefetch_shared": bool(args.prefetch_shared),
+                        "timing": f"CUDA-graph replay of the {launches_per_step(HEADLINE_T)}"
+                                  "-launch block, CUDA events"},
             "us_per_block": head["us_per_block"],
             "block_roofline": {"roofline_us": head["roofline_us"],
                                "frac": head["roofline_frac"],

@@ -50,7 +50,7 @@ def _worker(rank: int, world: int, port: int, T_by_rank, q, mode="dedup"):
         ep = ExpertParallelMoE(NumpyEPBackend(loc, d.E, world, rank, d.topk))
         res = {"dedup": ep.forward_dedup,
                "partial": lambda h, r: ep.forward_dedup(h, r, "partial"),
-               "pairs": ep.forward, "fixed": ep.forward_fixed}[mode](h, r)
+               "pairs": ep.forward_pairs, "fixed": ep.forward_fixed}[mode](h, r)
         res.setdefault("pairs_in", None)
         res.setdefault("rows_in", None)
         f = {k: (v.float().numpy() if v is not None else None) for k, v in full.items()}

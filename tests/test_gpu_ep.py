@@ -221,7 +221,7 @@ def test_ep_single_rank_matches_block(T, fixed):
     h, r = synth.make_inputs(31 + T, T, D, DEV)
     ref = blk(h, r)
     ep = ExpertParallelMoE(be)
-    res = ep.forward_fixed(h, r) if fixed else ep(h, r)
+    res = ep.forward_fixed(h, r) if fixed else ep.forward_pairs(h, r)
     finish()
     assert torch.equal(res["topi"], ref.topi)
     assert torch.equal(res["h1"].view(torch.int16), ref.h1.view(torch.int16))

@@ -128,3 +128,18 @@ def test_lazy_prenorm_exact_logits_match_reference():
     lz = O.lazy_router_logits(h, O.fold_weight_rowmajor(gw.T.copy(), w))
     rms = float(np.sqrt((ex.astype(np.float64) ** 2).mean()))
     assert float(np.abs(lz - ex).max()) <= 2e-2 * rms
+
+
+def test_numpy_generator_matches_library_bits():
+    """oracle/synth_np.py (the CPU arms' input generator, which loads no CUDA library)
+    gives the bits of the library's host generator for every stream, including a slice
+    taken from an element offset (one expert of the stacked weights)."""
+    from oracle import synth_np as S
+
+    for name, shape, off in (("h", (3, 6144), 0), ("r", (2, 512), 0), ("gamma", (6144,), 0),
+                             ("gate_w", (256, 64), 0), ("bias", (256,), 0),
+                             ("w13", (64, 96), 5 * 64 * 96), ("w2", (96, 32), 77),
+                             ("w13s", (16, 40), 0), ("w2s", (40, 8), 0)):
+        a = S.make(name, shape, 7, offset=off)
+        b = synth.make(name, shape, 7, offset=off).float().numpy()
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), name

@@ -62,6 +62,13 @@ extern "C" {
 #define FUS_GEMM_NO_PAIR 0x40     /* (first group) no SM-pair (2-CTA cluster, M = 256)     */
                                   /* tiles; by default persistent launches with 256-token  */
                                   /* blocks and dense outputs use them                     */
+#define FUS_GEMM_PAIR_SPLIT 0x80  /* (per group) SM-pair tiles never span an expert's two  */
+                                  /* token blocks (measurement switch; by default an      */
+                                  /* expert with exactly two blocks is one tile)          */
+#define FUS_GEMM_PAIR_V2 0x100    /* (first group) SM-pair kernel with tiles spanning an  */
+                                  /* expert's two blocks and SwiGLU gate/up rows stacked  */
+                                  /* in one accumulator (measurement switch; by default   */
+                                  /* one block per tile, gate and up accumulated apart)   */
 
 int fus_version(void);
 const char* fus_last_error(void);

@@ -219,20 +219,34 @@ def test_persistent_equals_one_tile_per_cta(bn, epi):
             assert rel_err(outs[0][0].float().cpu().numpy(), yref.cpu().numpy()) < 1e-2
 
 
+@pytest.mark.parametrize("layout", ["reference", "balanced"])
 @pytest.mark.parametrize("epi", ["swiglu", "bf16"])
-def test_pair_tiles_ragged_experts(epi):
+def test_pair_tiles_ragged_experts(epi, layout):
     """SM-pair tiles (2-CTA clusters, M = 256, each SM staging half of the token block)
     give the same bits as the single-CTA persistent kernel and as one tile per CTA, on
     expert blocks holding 1 .. 256 live tokens (token boxes of 16 / 64 / 128 rows per
     CTA), with a dense second group (fp32 output on the down projection); and match an
-    fp32 reference."""
-    counts = [1, 17, 100, 130, 256, 300, 513, 40]
+    fp32 reference. Experts with exactly two blocks (300, 257 and 511 tokens: one tile
+    over both blocks) and three (513), in the reference layout (full block + remainder)
+    and the balanced one; the expert-spanning pair kernel (with and without spanning)
+    gives the same bits too."""
+    counts = [1, 17, 100, 130, 256, 300, 513, 40, 257, 511]
     E, bn = len(counts), 256
     ids = np.concatenate([np.full(c, e, np.int32) for e, c in enumerate(counts)])
     ids = np.random.default_rng(5).permutation(ids)[:, None]
     T = ids.shape[0]
-    s_np, e_np, n_np = O.moe_align_block_size(ids, bn, E)
-    s, eids, ntp = (torch.from_numpy(v).to(DEV) for v in (s_np, e_np, n_np))
+    if layout == "reference":
+        s_np, e_np, n_np = O.moe_align_block_size(ids, bn, E)
+        s, eids, ntp = (torch.from_numpy(v).to(DEV) for v in (s_np, e_np, n_np))
+    else:
+        cap0 = (T + E * (bn - 1) + bn - 1) // bn * bn
+        # entries past the padded total are not written: pads and expert 0 there
+        s = torch.full((cap0,), T, dtype=torch.int32, device=DEV)
+        eids = torch.zeros(cap0 // bn, dtype=torch.int32, device=DEV)
+        ntp = torch.zeros(1, dtype=torch.int32, device=DEV)
+        ops.moe_align(torch.from_numpy(ids).to(DEV), E, bn, s, eids, ntp,
+                      flags=ops.ALIGN_BALANCED)
+        s_np = s.cpu().numpy()
     cap, R = s_np.size, T
     maxb = cap // bn
     if epi == "swiglu":
@@ -253,7 +267,8 @@ def test_pair_tiles_ragged_experts(epi):
         w_rows, K, n_out, epi_id, xin, xsh = H, I, H, ops.FUS_EPI_BF16, a, a_s
         fl = 0
     outs = []
-    for flag in (0, ops.GEMM_NO_PAIR, ops.GEMM_NO_PERSIST):
+    for flag in (0, ops.GEMM_PAIR_V2, ops.GEMM_PAIR_V2 | ops.GEMM_PAIR_SPLIT, ops.GEMM_NO_PAIR,
+                 ops.GEMM_NO_PERSIST):
         o = torch.zeros(cap, n_out, dtype=torch.bfloat16, device=DEV)
         # the shared group writes fp32 on the down projection (as the prefill block does)
         o_s = torch.zeros(T, n_out, dtype=torch.bfloat16 if epi == "swiglu" else torch.float32,

@@ -54,8 +54,6 @@ def parse():
     ap.add_argument("--strong", default="256,2048,8192,8192z",
                     help="N>1: global batch sizes split over the ranks (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--prefetch-shared", action="store_true",
-                    help="decode: the front end pulls the shared expert's weights into L2")
     ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1 decode row exchange: NVLink peer stores or NCCL all_to_all")
     return ap.parse_args()
@@ -468,8 +466,7 @@ def main() -> None:
 
     dims = synth.Dims()
     w = synth.make_block_weights(SEED, dims, "cuda")
-    blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"],
-                   prefetch_shared=args.prefetch_shared)
+    blk = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"], w["w2s"])
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     pk = traffic.peaks()
 
@@ -642,7 +639,6 @@ def main() -> None:
             "data": "synthetic (seeded Irwin-Hall normals, GLM-5.2 shapes, random-init weights)",
             "config": headline_config(1),
             "details": {"block_n": head["block_n"],
-                        "prefetch_shared": bool(args.prefetch_shared),
                         "timing": f"CUDA-graph replay of the {launches_per_step(HEADLINE_T)}"
                                   "-launch block, CUDA events"},
             "us_per_block": head["us_per_block"],

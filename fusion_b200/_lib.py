@@ -64,7 +64,6 @@ class MergeSpec(C.Structure):
     ]
 
 
-FUS_BLOCK_PREFETCH_SHARED = 0x1
 
 
 class BlockDesc(C.Structure):

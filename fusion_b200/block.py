@@ -31,13 +31,11 @@ class MoEBlock:
     """Holds device weights in the reference's layouts:
     gamma [H] bf16, gate_w [E,H] fp32 (or bf16), bias [E] fp32 | None,
     w13 [E,2I,H] bf16, w2 [E,H,I] bf16, shared w13s [2I,H] / w2s [H,I] bf16 | None.
-    n_group / topk_group > 1 select noaux_tc grouped routing (DeepSeek-V3-style).
-    prefetch_shared: at decode the front end also pulls the shared expert's weights into
-    L2 (FUS_BLOCK_PREFETCH_SHARED)."""
+    n_group / topk_group > 1 select noaux_tc grouped routing (DeepSeek-V3-style)."""
 
     def __init__(self, gamma, gate_w, bias, w13, w2, w13s=None, w2s=None, *, topk: int = 8,
                  eps: float = 1e-5, routed_scale: float = 2.5, renorm: bool = True,
-                 n_group: int = 1, topk_group: int = 1, prefetch_shared: bool = False):
+                 n_group: int = 1, topk_group: int = 1):
         self.E, twoI, self.H = w13.shape
         self.I = twoI // 2
         self.topk = topk
@@ -58,7 +56,7 @@ class MoEBlock:
         d.w13s = w13s.data_ptr() if w13s is not None else None
         d.w2s = w2s.data_ptr() if w2s is not None else None
         d.n_group, d.topk_group = n_group, topk_group  # noaux_tc grouping (1: GLM-5.2)
-        d.flags = L.FUS_BLOCK_PREFETCH_SHARED if prefetch_shared else 0
+        d.flags = 0
         self.desc = d
         self._ws: torch.Tensor | None = None
         self._graphs: dict[int, tuple] = {}

@@ -88,26 +88,6 @@ bool layout_for(const fus_moe_block_desc* d, int T, int bn, BlockLayout& L) {
   return true;
 }
 
-// the shared expert's weight regions the decode front end asks L2 for (none unless
-// FUS_BLOCK_PREFETCH_SHARED is set and the block has a shared expert)
-struct Prefetch {
-  const void* p0 = nullptr;
-  long b0 = 0;
-  const void* p1 = nullptr;
-  long b1 = 0;
-};
-
-Prefetch prefetch_for(const fus_moe_block_desc* d) {
-  Prefetch pf;
-  if (d->w13s && d->w2s && (d->flags & FUS_BLOCK_PREFETCH_SHARED)) {
-    pf.p0 = d->w13s;
-    pf.b0 = 2L * d->I * d->H * 2;
-    pf.p1 = d->w2s;
-    pf.b1 = (long)d->H * d->I * 2;
-  }
-  return pf;
-}
-
 }  // namespace
 
 using namespace fus;
@@ -145,11 +125,10 @@ extern "C" int fus_moe_block_check(const fus_moe_block_desc* d, int T, int block
   if (!layout_for(d, T, block_n, L)) return set_error(FUS_E_INVALID, "moe_block: bad sizes");
   if (ws_bytes < L.total)
     return set_error(FUS_E_INVALID, "moe_block: workspace %zu < %zu", ws_bytes, L.total);
-  if (small_path(d, T)) {
-    const Prefetch pf = prefetch_for(d);
+  if (d->flags) return set_error(FUS_E_INVALID, "moe_block: flags must be 0");
+  if (small_path(d, T))
     return route_small_check(T, d->H, d->E, d->topk, d->n_group, d->topk_group, block_n,
-                             d->nplanes, pf.p0, pf.b0, pf.p1, pf.b1);
-  }
+                             d->nplanes);
   return FUS_OK;
 }
 
@@ -186,14 +165,12 @@ extern "C" int fus_moe_block_forward(const fus_moe_block_desc* d, const void* h,
   int rc;
   const bool small = small_path(d, T);
   if (small) {
-    const Prefetch pf = prefetch_for(d);
     // decode: norm + router + top-k + layout in one launch; it also clears the merge
     // counters, so the down projection needs no separate reset
     if ((rc = route_small_launch(h, r, d->gamma, d->eps, d->wa, d->nplanes, d->bias, T, H, E, K,
                                  d->routed_scale, d->renorm, d->n_group, d->topk_group, h1, x2,
                                  partial, topw, topi, block_n, sorted, L.cap, eids, L.blocks_cap,
-                                 ntp, done, counters, T * L.tiles, stream, status,
-                                 pf.p0, pf.b0, pf.p1, pf.b1)))
+                                 ntp, done, counters, T * L.tiles, stream, status)))
       return rc;
   } else {
     if ((rc = fus_add_rmsnorm(h, H, r, H, d->gamma, h1, H, x2, H, T, H, d->eps, 1, 1, stream,

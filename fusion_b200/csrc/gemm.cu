@@ -499,7 +499,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 #include "gemm_persist.cuh"
 #include "gemm_pair.cuh"
-#include "gemm_pair2.cuh"
 
 // ======================================================================================
 // host side
@@ -555,19 +554,6 @@ int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStre
   grouped_gemm_pair<EPI><<<(int)(2 * clusters), kPThreads, Cfg::SMEM_BYTES, st>>>(
       maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[4], maps[5], a);
   return check_launch("grouped_gemm_pair");
-}
-
-template <int EPI>
-int launch_pair2(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStream_t st) {
-  using Cfg = Pair2Cfg<EPI>;
-  if (int rc = ensure_smem_attr((const void*)grouped_gemm_pair2<EPI>, Cfg::SMEM_BYTES,
-                                 "grouped_gemm_pair2"))
-    return rc;
-  long clusters = num_sms() / 2;
-  if (clusters > total) clusters = total;
-  grouped_gemm_pair2<EPI><<<(int)(2 * clusters), kPThreads, Cfg::SMEM_BYTES, st>>>(
-      maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[4], maps[5], a);
-  return check_launch("grouped_gemm_pair2");
 }
 
 template <int BN, int EPI, int MT>
@@ -805,24 +791,15 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
       const fus_gemm_group& G = groups[g];
       pair = !G.gather_ids && !G.row_map && !G.row_scale && !G.res && G.row_limit >= 1;
     }
-    const bool v1 = !(groups[0].flags & FUS_GEMM_PAIR_V2);
-    if (pair && epilogue == FUS_EPI_SWIGLU && !v1 && w_rows % 256) pair = false;
     if (pair) {
-      // pair2 SwiGLU tiles: 128 output features (64 gate + 64 up weight rows per CTA)
-      const bool v2s = !v1 && epilogue == FUS_EPI_SWIGLU;
-      a.m_tiles = epilogue == FUS_EPI_SWIGLU ? (v1 ? w_rows / 512 : w_rows / 256) : w_rows / 256;
+      a.m_tiles = epilogue == FUS_EPI_SWIGLU ? w_rows / 512 : w_rows / 256;
       long pu[2] = {0, 0};
       for (int g = 0; g < ngroups; ++g) {
         const fus_gemm_group& G = groups[g];
         pu[g] = (long)G.max_blocks * a.m_tiles;
         const bool out32 = epilogue == FUS_EPI_BF16 && (G.flags & FUS_GEMM_OUT_F32);
         int rc = make_tmap_store_2d(&maps[4 + g], G.out, out32, (uint64_t)out_cols,
-                                    (uint64_t)G.row_limit, (uint64_t)G.ldo, v2s ? 64 : 128,
-                                    out32 ? 16 : 32);
-        // weights: 64-row boxes (gate and up halves of a stacked operand) for pair2 SwiGLU
-        if (!rc && v2s)
-          rc = make_tmap_bf16_2d(&maps[g], G.w, (uint64_t)K, (uint64_t)G.n_experts * w_rows,
-                                 (uint64_t)K, kBK, 64);
+                                    (uint64_t)G.row_limit, (uint64_t)G.ldo, 128, out32 ? 16 : 32);
         // token maps: boxes of 128 / 16 / 64 rows (one CTA's half of a block)
         if (!rc)
           rc = make_tmap_bf16_2d(&maps[2 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
@@ -837,7 +814,6 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
         a.g[g].tma_store = 1;
       }
       if (ngroups == 1) {
-        maps[1] = maps[0];
         maps[3] = maps[2];
         maps[5] = maps[4];
         maps[7] = maps[6];
@@ -846,9 +822,6 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
       const long ptotal = pu[0] + pu[1];
       if (ptotal > 0x7fffffffL) return set_error(FUS_E_UNSUPPORTED, "grid too large");
       a.units0 = (int)pu[0];
-      if (!v1)
-        return epilogue == FUS_EPI_SWIGLU ? launch_pair2<FUS_EPI_SWIGLU>(maps, a, ptotal, st)
-                                          : launch_pair2<FUS_EPI_BF16>(maps, a, ptotal, st);
       return epilogue == FUS_EPI_SWIGLU ? launch_pair<FUS_EPI_SWIGLU>(maps, a, ptotal, st)
                                         : launch_pair<FUS_EPI_BF16>(maps, a, ptotal, st);
     }
@@ -888,11 +861,3 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
     default: return launch_bn<FUS_EPI_F32>(block_n, mt2, maps, a, (int)total, st);
   }
 }
-
-#ifdef FUS_PAIR2_TRACE
-// phase counters of the last two pair2 launches (w13 into set 0, w2 into set 1)
-extern "C" int fus_pair2_trace(int sel, unsigned long long* host) {
-  if (sel >= 0) return cudaMemcpyToSymbol(fus::g_pair2_trace_sel, &sel, sizeof(int)) != cudaSuccess;
-  return cudaMemcpyFromSymbol(host, fus::g_pair2_trace, sizeof(fus::g_pair2_trace)) != cudaSuccess;
-}
-#endif

@@ -61,14 +61,12 @@ int route_small_launch(const void* h, const void* r, const void* gamma, float ep
                        int renorm, int n_group, int topk_group, void* h1, void* x2, float* logits,
                        float* topw, int* topi, int block_m, int* sorted_ids, int sorted_cap,
                        int* expert_ids, int blocks_cap, int* ntp, int* done, int* zero,
-                       int zero_n, void* stream, int* status, const void* pf0 = nullptr,
-                       long pf0_bytes = 0, const void* pf1 = nullptr, long pf1_bytes = 0);
+                       int zero_n, void* stream, int* status);
 
-// route_small_launch's shape and prefetch-region checks, without pointers to device data
+// route_small_launch's shape checks, without pointers to device data
 // (host only: fus_moe_block_check runs it on the CPU with the block's own arguments)
 int route_small_check(int T, int H, int E, int topk, int n_group, int topk_group, int block_m,
-                      int nplanes, const void* pf0, long pf0_bytes, const void* pf1,
-                      long pf1_bytes);
+                      int nplanes);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

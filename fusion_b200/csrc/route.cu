@@ -46,12 +46,8 @@ struct RouteArgs {
   int* done;
   int* zero;
   int zero_n;
-  const uint8_t* pf[2];  // regions prefetched into L2 while the CTAs route (or null)
-  long pf_bytes[2];
   int* status;
 };
-
-constexpr long kPrefetchChunk = 64 * 1024;
 
 __global__ void __launch_bounds__(kRouteThreads)
     route_small_kernel(const __grid_constant__ RouteArgs a) {
@@ -80,19 +76,6 @@ __global__ void __launch_bounds__(kRouteThreads)
         wq[ci][p] = __ldg(reinterpret_cast<const uint4*>(a.wa + (long)e0 * a.nplanes * H +
                                                          (long)p * H + c * 8));
     if (c < nv) gq[ci] = __ldg(reinterpret_cast<const uint4*>(a.gamma) + c);
-  }
-  // weights the next launches read whatever the routing decides (the shared expert):
-  // each CTA asks for its slice of them in L2 now, while HBM would otherwise idle under
-  // this latency-bound kernel
-  if (tid == 0) {
-    for (int q = 0; q < 2; ++q) {
-      const long nb = a.pf_bytes[q];
-      if (nb <= 0) continue;
-      const long per = ((nb + gridDim.x - 1) / gridDim.x + 15) & ~15L;
-      const long b1 = min(nb, per * (blockIdx.x + 1));
-      for (long b = per * blockIdx.x; b < b1; b += kPrefetchChunk)
-        l2_prefetch_bulk(a.pf[q] + b, (uint32_t)min(kPrefetchChunk, b1 - b));
-    }
   }
   // the correction bias of experts lane*8 .. lane*8+7, for the selection (whichever CTA
   // turns out to be the last one needs it; loading it now takes it off the tail)
@@ -343,13 +326,9 @@ using namespace fus;
 
 namespace fus {
 int route_small_check(int T, int H, int E, int topk, int n_group, int topk_group, int block_m,
-                      int nplanes, const void* pf0, long pf0_bytes, const void* pf1,
-                      long pf1_bytes) {
+                      int nplanes) {
   if (n_group < 1) n_group = 1;
   if (topk_group < 1) topk_group = 1;
-  if ((pf0_bytes > 0 && (!pf0 || pf0_bytes % 16 || !aligned16(pf0))) ||
-      (pf1_bytes > 0 && (!pf1 || pf1_bytes % 16 || !aligned16(pf1))))
-    return set_error(FUS_E_INVALID, "route_small: prefetch regions must be 16-byte granular");
   if (n_group > 1 && (E % n_group || (E / n_group) % 8 ||
                       ((E / n_group / 8) & (E / n_group / 8 - 1)) || n_group > 32 ||
                       topk_group > n_group || topk > topk_group * (E / n_group)))
@@ -370,10 +349,8 @@ int route_small_launch(const void* h, const void* r, const void* gamma, float ep
                        int renorm, int n_group, int topk_group, void* h1, void* x2, float* logits,
                        float* topw, int* topi, int block_m, int* sorted_ids, int sorted_cap,
                        int* expert_ids, int blocks_cap, int* ntp, int* done, int* zero,
-                       int zero_n, void* stream, int* status, const void* pf0, long pf0_bytes,
-                       const void* pf1, long pf1_bytes) {
-  if (int rc = route_small_check(T, H, E, topk, n_group, topk_group, block_m, nplanes, pf0,
-                                 pf0_bytes, pf1, pf1_bytes))
+                       int zero_n, void* stream, int* status) {
+  if (int rc = route_small_check(T, H, E, topk, n_group, topk_group, block_m, nplanes))
     return rc;
   if (n_group < 1) n_group = 1;
   if (topk_group < 1) topk_group = 1;
@@ -419,10 +396,6 @@ int route_small_launch(const void* h, const void* r, const void* gamma, float ep
   a.done = done;
   a.zero = zero;
   a.zero_n = zero_n;
-  a.pf[0] = (const uint8_t*)pf0;
-  a.pf[1] = (const uint8_t*)pf1;
-  a.pf_bytes[0] = pf0 ? pf0_bytes : 0;
-  a.pf_bytes[1] = pf1 ? pf1_bytes : 0;
   a.status = status;
   route_small_kernel<<<E / kRouteExperts, kRouteThreads, dyn, as_stream(stream)>>>(a);
   return check_launch("route_small");

@@ -62,13 +62,6 @@ extern "C" {
 #define FUS_GEMM_NO_PAIR 0x40     /* (first group) no SM-pair (2-CTA cluster, M = 256)     */
                                   /* tiles; by default persistent launches with 256-token  */
                                   /* blocks and dense outputs use them                     */
-#define FUS_GEMM_PAIR_SPLIT 0x80  /* (per group) SM-pair tiles never span an expert's two  */
-                                  /* token blocks (measurement switch; by default an      */
-                                  /* expert with exactly two blocks is one tile)          */
-#define FUS_GEMM_PAIR_V2 0x100    /* (first group) SM-pair kernel with tiles spanning an  */
-                                  /* expert's two blocks and SwiGLU gate/up rows stacked  */
-                                  /* in one accumulator (measurement switch; by default   */
-                                  /* one block per tile, gate and up accumulated apart)   */
 
 int fus_version(void);
 const char* fus_last_error(void);
@@ -390,13 +383,8 @@ typedef struct fus_moe_block_desc {
   const void* w2s;    /* shared expert [H, I] bf16 or NULL        */
   int n_group;        /* noaux_tc groups (0 or 1: none; GLM-5.2)  */
   int topk_group;     /* groups kept when n_group > 1             */
-  int flags;          /* FUS_BLOCK_* options (0: none)            */
+  int flags;          /* reserved, must be 0                      */
 } fus_moe_block_desc;
-
-/* Block option: at decode, the front end (norm + router + top-k) also asks for the shared
- * expert's weights in L2, so that the expert GEMMs read that part from L2 instead of
- * HBM (the front end is latency-bound and leaves HBM idle). */
-#define FUS_BLOCK_PREFETCH_SHARED 0x1
 
 int fus_moe_block_pick_block_n(int T, int E, int topk);
 size_t fus_moe_block_workspace(const fus_moe_block_desc* d, int T, int block_n);

@@ -83,18 +83,17 @@ def _glm_desc(shared: bool, flags: int) -> L.BlockDesc:
 
 
 def test_block_check_accepts_default_calls_at_every_size():
-    """The block's pre-launch checks pass for the default descriptor (prefetch off) at
-    decode and prefill sizes, with and without the shared expert: a decode call whose
-    front end would reject its own arguments fails here, on the CPU."""
+    """The block's pre-launch checks pass for the default descriptor at decode and
+    prefill sizes, with and without the shared expert: a decode call whose front end
+    would reject its own arguments fails here, on the CPU."""
     lib = L.lib()
     for shared in (True, False):
-        for flags in (0, L.FUS_BLOCK_PREFETCH_SHARED):
-            d = _glm_desc(shared, flags)
-            for T in (1, 2, 8, 16, 17, 32, 256, 2048, 8192):
-                bn = lib.fus_moe_block_pick_block_n(T, 256, 8)
-                ws = lib.fus_moe_block_workspace(ctypes.byref(d), T, bn)
-                rc = lib.fus_moe_block_check(ctypes.byref(d), T, 0, ws)
-                assert rc == 0, (shared, flags, T, L.last_error())
+        d = _glm_desc(shared, 0)
+        for T in (1, 2, 8, 16, 17, 32, 256, 2048, 8192):
+            bn = lib.fus_moe_block_pick_block_n(T, 256, 8)
+            ws = lib.fus_moe_block_workspace(ctypes.byref(d), T, bn)
+            rc = lib.fus_moe_block_check(ctypes.byref(d), T, 0, ws)
+            assert rc == 0, (shared, T, L.last_error())
 
 
 def test_block_check_rejects_bad_arguments():
@@ -106,10 +105,12 @@ def test_block_check_rejects_bad_arguments():
     d.w2s = None  # shared gate-up without shared down
     assert lib.fus_moe_block_check(ctypes.byref(d), 1, 0, ws) == -1
     assert "missing weights" in L.last_error()
-    d = _glm_desc(True, L.FUS_BLOCK_PREFETCH_SHARED)
-    d.w13s = ctypes.c_void_p(0xA0008)  # prefetch region not 16-byte aligned
+    d = _glm_desc(True, 1)  # the flags field is reserved
     assert lib.fus_moe_block_check(ctypes.byref(d), 1, 0, ws) == -1
-    assert "16-byte" in L.last_error()
+    assert "flags" in L.last_error()
+    d = _glm_desc(True, 0)
+    d.topk = 40  # 40 slots per token: past the decode front end's limit
+    assert lib.fus_moe_block_check(ctypes.byref(d), 4, 16, 1 << 40) != 0
     assert lib.fus_moe_block_check(ctypes.byref(_glm_desc(True, 0)), 0, 0, 0) == 0
 
 

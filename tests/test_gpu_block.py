@@ -149,27 +149,6 @@ def test_block_graph_replay_matches_eager(weights_404):
     assert torch.equal(outs.topi, eager.topi)
 
 
-@pytest.mark.parametrize("T", [1, 8])
-def test_prefetch_shared_changes_no_bits(weights_404, T):
-    """FUS_BLOCK_PREFETCH_SHARED only moves the shared expert's weights into L2 during the
-    decode front end: same outputs, eager and graph-replayed."""
-    w = weights_404
-    blk = make_block(w)
-    blk_pf = MoEBlock(w["gamma"], w["gate_w"], w["bias"], w["w13"], w["w2"], w["w13s"],
-                      w["w2s"], prefetch_shared=True)
-    h, r = synth.make_inputs(91 + T, T, D, DEV)
-    ref = blk(h, r)
-    got = blk_pf(h, r)
-    g, hin, rin, outs, _ = blk_pf.capture(T)
-    hin.copy_(h)
-    rin.copy_(r)
-    g.replay()
-    finish()
-    for o in (got, outs):
-        assert torch.equal(o.out.view(torch.int16), ref.out.view(torch.int16))
-        assert torch.equal(o.topi, ref.topi)
-
-
 @pytest.mark.parametrize("T", [3, 16])
 def test_fused_merge_matches_merge_kernel_and_rearms(weights_404, T):
     """The w2 epilogue's last-arriver merge equals the standalone merge kernel bit for

@@ -49,8 +49,19 @@ struct RouteArgs {
   int* status;
 };
 
+// Optional phase timestamps (globaltimer ns), compiled only with FUS_ROUTE_TRACE:
+// [0] earliest CTA start, [1] latest CTA at the ticket, [2] CTA 0 after the norm,
+// [3] CTA 0 after the logits, [4] last CTA after selection, [5] last CTA done.
+#ifdef FUS_ROUTE_TRACE
+__device__ unsigned long long g_route_trace[8];
+#define RT(...) __VA_ARGS__
+#else
+#define RT(...)
+#endif
+
 __global__ void __launch_bounds__(kRouteThreads)
     route_small_kernel(const __grid_constant__ RouteArgs a) {
+  RT(if (threadIdx.x == 0) atomicMin(&g_route_trace[0], globaltimer_ns());)
   extern __shared__ __align__(16) uint8_t dsm[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(dsm);  // [T][H]: h1, then x2
   __shared__ float rstd_s[kRouteMaxT];
@@ -137,6 +148,7 @@ __global__ void __launch_bounds__(kRouteThreads)
     }
   }
   __syncthreads();
+  RT(if (threadIdx.x == 0 && blockIdx.x == 0) g_route_trace[2] = globaltimer_ns();)
   // ---- 3. logits of expert e0 (fp32 FMAs over the reassembled fp32 weight) ----
   float acc[kRouteExperts][kRouteMaxT];
 #pragma unroll
@@ -187,9 +199,11 @@ __global__ void __launch_bounds__(kRouteThreads)
       a.logits[(long)t * E + e0 + e] = v;
     }
   }
+  RT(if (threadIdx.x == 0 && blockIdx.x == 0) g_route_trace[3] = globaltimer_ns();)
   // ---- 4. ticket: the last CTA selects and lays out ----
   __threadfence();
   __syncthreads();
+  RT(if (threadIdx.x == 0) atomicMax(&g_route_trace[1], globaltimer_ns());)
   if (tid == 0) is_last = atomicAdd(a.done, 1) == (int)gridDim.x - 1;
   __syncthreads();
   if (!is_last) return;
@@ -218,50 +232,49 @@ __global__ void __launch_bounds__(kRouteThreads)
         ix[j] = 0x7fffffff;
       }
     }
+    RT(if (lane == 0 && t == 0) g_route_trace[6] = globaltimer_ns();)
     group_mask_choice(ch, lane, E, a.n_group, a.topk_group);
-    // sort the lane's 8 descending by (ch, then lower expert id): odd-even transposition
+    // order-preserving unsigned keys of the choice values (descending choice, then the
+    // lower expert id): each round takes the warp's best with two redux.sync maxima
+    // (key, then 0xffff - id among the lanes holding that key), and the winner's lane
+    // drops it and re-takes its own best of 8
+    uint32_t key[8];
 #pragma unroll
-    for (int pass = 0; pass < 8; ++pass)
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t u = __float_as_uint(ch[j] + 0.0f);  // -0 (a masked choice) as +0
+      key[j] = ix[j] == 0x7fffffff ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+    }
+    auto lane_best = [&](uint32_t& bk, int& bj) {
+      bk = key[0];
+      bj = 0;
 #pragma unroll
-      for (int j = pass & 1; j + 1 < 8; j += 2) {
-        const bool sw = ch[j + 1] > ch[j] || (ch[j + 1] == ch[j] && ix[j + 1] < ix[j]);
-        if (sw) {
-          const float tc = ch[j], ts = sc[j];
-          const int ti = ix[j];
-          ch[j] = ch[j + 1];
-          sc[j] = sc[j + 1];
-          ix[j] = ix[j + 1];
-          ch[j + 1] = tc;
-          sc[j + 1] = ts;
-          ix[j + 1] = ti;
+      for (int j = 1; j < 8; ++j)
+        if (key[j] > bk) {  // strict: equal keys keep the lower index (lower expert id)
+          bk = key[j];
+          bj = j;
         }
-      }
-    // topk rounds: the warp's best head wins (ties -> lower expert id), its lane pops it
+    };
+    uint32_t bk;
+    int bj;
+    lane_best(bk, bj);
+    RT(if (lane == 0 && t == 0) g_route_trace[7] = globaltimer_ns();)
     float my_w = 0.f, wsum = 0.f;
     int my_id = 0;
     for (int k = 0; k < a.topk; ++k) {
-      float bv = ch[0];
-      int bi = ix[0];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
+      const uint32_t top = __reduce_max_sync(0xffffffffu, bk);
+      const uint32_t lo = __reduce_max_sync(0xffffffffu, bk == top ? 0xffffu - (uint32_t)(e8 + bj) : 0u);
+      const int bi = 0xffff - (int)lo;
       const int owner = bi >> 3;
-      const float s_win = __shfl_sync(0xffffffffu, sc[0], owner & 31);
+      float s_mine = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j == bj) s_mine = sc[j];
+      const float s_win = __shfl_sync(0xffffffffu, s_mine, owner);
       if (lane == owner) {
 #pragma unroll
-        for (int j = 0; j < 7; ++j) {
-          ch[j] = ch[j + 1];
-          sc[j] = sc[j + 1];
-          ix[j] = ix[j + 1];
-        }
-        ch[7] = -INFINITY;
-        ix[7] = 0x7fffffff;
+        for (int j = 0; j < 8; ++j)
+          if (j == bj) key[j] = 0u;
+        lane_best(bk, bj);
       }
       wsum += s_win;
       if (lane == k) {
@@ -278,6 +291,7 @@ __global__ void __launch_bounds__(kRouteThreads)
       ids_s[t * a.topk + lane] = my_id;
     }
   }
+  RT(__syncthreads(); if (threadIdx.x == 0) g_route_trace[4] = globaltimer_ns();)
   // dispatch layout over the T*topk flat indices (stable by flat index)
   const int numel = T * a.topk;
   for (int e = tid; e < 256; e += kRouteThreads) cnt[e] = 0;
@@ -286,16 +300,23 @@ __global__ void __launch_bounds__(kRouteThreads)
   __syncthreads();
   const int bm = a.block_m;
   const int padded = tid < E ? (cnt[tid] + bm - 1) / bm * bm : 0;
-  scan[tid] = padded;
-  __syncthreads();
-  for (int off = 1; off < kRouteThreads; off <<= 1) {
-    const int v = tid >= off ? scan[tid - off] : 0;
-    __syncthreads();
-    scan[tid] += v;
-    __syncthreads();
+  // inclusive scan of the padded counts: within each warp by shuffles, then over the
+  // eight warp totals
+  int incl = padded;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
   }
-  const int incl = scan[tid];
-  const int total = scan[kRouteThreads - 1];
+  if (lane == 31) scan[warp] = incl;
+  __syncthreads();
+  int total = 0;
+#pragma unroll
+  for (int w = 0; w < kRouteThreads / 32; ++w) {
+    const int v = scan[w];
+    if (w < warp) incl += v;
+    total += v;
+  }
   if (tid < E) start[tid] = incl - padded;
   if (tid == 0) {
     a.ntp[0] = total;
@@ -318,6 +339,7 @@ __global__ void __launch_bounds__(kRouteThreads)
   }
   for (int i = tid; i < a.zero_n; i += kRouteThreads) a.zero[i] = 0;
   if (tid == 0) *a.done = 0;  // re-arm the ticket
+  RT(__syncthreads(); if (threadIdx.x == 0) g_route_trace[5] = globaltimer_ns();)
 }
 
 }  // namespace fus
@@ -413,3 +435,13 @@ extern "C" int fus_moe_route_small(const void* h, const void* r, const void* gam
                             1, h1, x2, logits, topw, topi, block_m, sorted_ids, sorted_cap,
                             expert_ids, blocks_cap, ntp, done, zero, zero_n, stream, status);
 }
+
+#ifdef FUS_ROUTE_TRACE
+extern "C" int fus_route_trace(int reset, unsigned long long* host) {
+  if (reset) {
+    unsigned long long init[8] = {~0ull, 0, 0, 0, 0, 0, 0, 0};
+    return cudaMemcpyToSymbol(fus::g_route_trace, init, sizeof(init)) != cudaSuccess;
+  }
+  return cudaMemcpyFromSymbol(host, fus::g_route_trace, sizeof(fus::g_route_trace)) != cudaSuccess;
+}
+#endif

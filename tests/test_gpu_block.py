@@ -113,7 +113,8 @@ def torch_block_exact(w, x2, h1, topw, topi):
     return out + h1.float() + s
 
 
-@pytest.mark.parametrize("T,zipf", [(256, False), (2048, False), (2048, True)])
+@pytest.mark.parametrize("T,zipf", [(256, False), (2048, False), (2048, True), (8192, False),
+                                    (8192, True)])
 def test_block_large_vs_torch_fp32(weights_404, T, zipf):
     if zipf:  # BASELINE config 4 routing skew: a few experts get hundreds of tokens
         weights_404 = dict(weights_404, bias=synth.zipf_bias(DEV))

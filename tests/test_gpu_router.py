@@ -91,14 +91,19 @@ def test_router_grouped_golden():
         np.testing.assert_allclose(tw.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
 
 
-@pytest.mark.parametrize("T", [1, 33, 256, 2048])
+@pytest.mark.parametrize("T", [1, 33, 256, 2048, 8192])
 def test_router_vs_oracle(T):
     x2 = synth.make("h", (T, 6144), 21 + T, DEV)
     gw = synth.make("gate_w", (256, 6144), 21, DEV)
     bias = synth.make("bias", (256,), 21, DEV)
     lg, tw, ti = gpu_router(x2, gw, bias)
     olg = O.router_logits(to_np(x2), to_np(gw))
-    np.testing.assert_allclose(lg, olg, rtol=0, atol=5e-5)
+    # two fp32 dot products of length H summed in different orders: each is within
+    # H*u*sum|x w| of the exact value (u = 2^-24); the bar is 32*u*sum|x w| (about 1.5e-4
+    # here), plus 5e-5 for logits whose terms cancel
+    mag = np.abs(to_np(x2)) @ np.abs(to_np(gw)).T
+    err = np.abs(lg - olg)
+    assert np.all(err <= 5e-5 + 32 * 2.0**-24 * mag), float((err - 32 * 2.0**-24 * mag).max())
     ow, oi = O.router_select(olg, to_np(bias))
     check_ids(ti, oi, olg, to_np(bias))
     same = np.all(ti == oi, axis=1)

@@ -580,6 +580,10 @@ def main() -> None:
                 "frac": achieved / pk.hbm_gbs, "peak_source": pk.source,
                 "algorithmic_bytes": w13_bytes, "avg_launch_us": w13_ms * 1e3,
                 "traffic": traffic_bytes,
+                "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum of this kernel "
+                                   "from the committed ncu capture profiles/"
+                                   "w13_swiglu_decode_T1.txt (same launch shape), not "
+                                   "measured in this run") if traffic_bytes else None,
                 "per_kernel_us": {k: v * 1e3 for k, v in kt.items()}}
 
     # ---- e2e through the public API with pinned host buffers ----

@@ -516,10 +516,10 @@ def main() -> None:
                 "roofline_us": t_roof * 1e6, "roofline_frac": t_roof / (ms_step / 1e3),
                 "algorithmic_GB": b / 1e9, "GFLOP": f / 1e9}
 
-    def kernel_times(T: int, reps: int = 20) -> dict:
-        """Per-kernel device time: each step of the chain (same kernels as the block) is
-        captured `reps` times back to back in its own CUDA graph and replayed once; the
-        replay's CUDA-event time / reps is the launch's steady-state duration."""
+    def kernel_times(T: int, reps: int = 30) -> dict:
+        """Per-kernel device time: each step of the chain (same kernels as the block) runs
+        alone after an L2 flush, bracketed by CUDA events on its stream; the median over
+        `reps` launches is the launch's duration."""
         ch = BlockChain(blk, T)
         h, r = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cuda")
         steps = ch.steps(h, r)
@@ -528,29 +528,18 @@ def main() -> None:
                 fn()
         torch.cuda.synchronize()
         ops.check_status()
-        out = {}
-        for n, fn in steps:
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(s):
-                fn()
-            torch.cuda.current_stream().wait_stream(s)
-            with torch.cuda.graph(g):
-                for _ in range(reps):
-                    fn()
-            times = []
-            for _ in range(3):
+        times = {n: [] for n, _ in steps}
+        for _ in range(reps):
+            for n, fn in steps:  # in block order: each step reads what the previous wrote
                 flush.zero_()
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record()
-                g.replay()
+                fn()
                 b.record()
-                torch.cuda.synchronize()
-                times.append(a.elapsed_time(b) / reps)
-            out[n] = statistics.median(times)
+                times[n].append((a, b))
+        torch.cuda.synchronize()
         ops.check_status()
-        return out, ch
+        return {n: statistics.median(a.elapsed_time(b) for a, b in v) for n, v in times.items()}, ch
 
     with ClockSampler(local) as clk:
         head = measure(HEADLINE_T, args.steps, max(args.warmup, 3))
@@ -584,7 +573,9 @@ def main() -> None:
                                    "from the committed ncu capture profiles/"
                                    "w13_swiglu_decode_T1.txt (same launch shape), not "
                                    "measured in this run") if traffic_bytes else None,
-                "per_kernel_us": {k: v * 1e3 for k, v in kt.items()}}
+                "per_kernel_us": {k: v * 1e3 for k, v in kt.items()},
+                "kernel_timing": "median of 30 launches of each step of the block's chain, "
+                                 "each alone after an L2 flush, CUDA events on its stream"}
 
     # ---- e2e through the public API with pinned host buffers ----
     T = HEADLINE_T

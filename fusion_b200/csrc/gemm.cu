@@ -527,10 +527,10 @@ int launch_persist(int bn, const CUtensorMap* maps, const GemmArgs& a, int grid,
   return set_error(FUS_E_UNSUPPORTED, "persistent GEMM: block_n %d", bn);
 }
 
-template <int EPI>
+template <int EPI, int NA>
 int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStream_t st) {
-  using Cfg = PairCfg<EPI>;
-  if (int rc = ensure_smem_attr((const void*)grouped_gemm_pair<EPI>, Cfg::SMEM_BYTES,
+  using Cfg = PairCfg<EPI, NA>;
+  if (int rc = ensure_smem_attr((const void*)grouped_gemm_pair<EPI, NA>, Cfg::SMEM_BYTES,
                                  "grouped_gemm_pair"))
     return rc;
   // co-resident cluster count (same on every B200; computed on the first device used)
@@ -541,7 +541,7 @@ int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStre
     cfg.gridDim = dim3(2 * (num_sms() / 2));
     cfg.blockDim = dim3(kPThreads);
     cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-    if (cudaOccupancyMaxActiveClusters(&max_clusters, grouped_gemm_pair<EPI>, &cfg) !=
+    if (cudaOccupancyMaxActiveClusters(&max_clusters, grouped_gemm_pair<EPI, NA>, &cfg) !=
         cudaSuccess) {
       (void)cudaGetLastError();
       max_clusters = 0;
@@ -551,7 +551,7 @@ int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStre
   // queue behind the first wave
   long clusters = max_clusters > 0 ? max_clusters : num_sms() / 2;
   if (clusters > total) clusters = total;
-  grouped_gemm_pair<EPI><<<(int)(2 * clusters), kPThreads, Cfg::SMEM_BYTES, st>>>(
+  grouped_gemm_pair<EPI, NA><<<(int)(2 * clusters), kPThreads, Cfg::SMEM_BYTES, st>>>(
       maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[4], maps[5], a);
   return check_launch("grouped_gemm_pair");
 }
@@ -792,7 +792,12 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
       pair = !G.gather_ids && !G.row_map && !G.row_scale && !G.res && G.row_limit >= 1;
     }
     if (pair) {
-      a.m_tiles = epilogue == FUS_EPI_SWIGLU ? w_rows / 512 : w_rows / 256;
+      // BF16 tiles of 512 rows when the rows divide: two weight tiles per CTA share each
+      // staged token tile, so a stage carries twice the MMA work for 1.5x the bytes (on
+      // ~150-token blocks the 256-row tile is bound by operand delivery)
+      const bool wide = epilogue == FUS_EPI_BF16 && w_rows % 512 == 0 &&
+                        !(groups[0].flags & FUS_GEMM_PAIR_NARROW);
+      a.m_tiles = (epilogue == FUS_EPI_SWIGLU || wide) ? w_rows / 512 : w_rows / 256;
       long pu[2] = {0, 0};
       for (int g = 0; g < ngroups; ++g) {
         const fus_gemm_group& G = groups[g];
@@ -822,8 +827,9 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
       const long ptotal = pu[0] + pu[1];
       if (ptotal > 0x7fffffffL) return set_error(FUS_E_UNSUPPORTED, "grid too large");
       a.units0 = (int)pu[0];
-      return epilogue == FUS_EPI_SWIGLU ? launch_pair<FUS_EPI_SWIGLU>(maps, a, ptotal, st)
-                                        : launch_pair<FUS_EPI_BF16>(maps, a, ptotal, st);
+      if (epilogue == FUS_EPI_SWIGLU) return launch_pair<FUS_EPI_SWIGLU, 2>(maps, a, ptotal, st);
+      return wide ? launch_pair<FUS_EPI_BF16, 2>(maps, a, ptotal, st)
+                  : launch_pair<FUS_EPI_BF16, 1>(maps, a, ptotal, st);
     }
     const int grid = (int)(total < sms ? total : sms);
     for (int g = 0; g < ngroups; ++g) {

@@ -99,9 +99,11 @@ FUS_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, uint32_t ba
 
 constexpr int kPairBN = 256;  // token rows per block (both CTAs)
 
-template <int EPI>
+// NA = 128-row weight tiles per CTA and stage, each with its own accumulator and all
+// multiplied by the same token tile (SwiGLU: gate + up; BF16: 1, or 2 for 512-row tiles)
+template <int EPI, int NA_ = (EPI == FUS_EPI_SWIGLU ? 2 : 1)>
 struct PairCfg {
-  static constexpr int NA = EPI == FUS_EPI_SWIGLU ? 2 : 1;  // weight tiles per CTA and stage
+  static constexpr int NA = NA_;
   static constexpr int A_BYTES = NA * kATileBytes;
   static constexpr int B_BYTES = (kPairBN / 2) * kBK * 2;  // this CTA's half of the tokens
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -117,7 +119,7 @@ struct PairCfg {
   static_assert(NBUF * ACC_COLS <= TMEM_COLS, "tensor memory");
 };
 
-template <int EPI>
+template <int EPI, int NA>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     grouped_gemm_pair(const __grid_constant__ CUtensorMap ta0,
                       const __grid_constant__ CUtensorMap ta1,
@@ -130,8 +132,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                       const __grid_constant__ CUtensorMap to0,
                       const __grid_constant__ CUtensorMap to1,
                       const __grid_constant__ GemmArgs args) {
-  using Cfg = PairCfg<EPI>;
+  using Cfg = PairCfg<EPI, NA>;
   constexpr int STAGES = Cfg::STAGES;
+  static_assert(EPI != FUS_EPI_SWIGLU || NA == 2, "SwiGLU pairs gate and up tiles");
   extern __shared__ uint8_t smem_raw[];
   // the same offsets in both CTAs: the dynamic window starts at the same address in each
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -203,8 +206,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const uint64_t pol_w = (G.flags & FUS_GEMM_W_STREAM) ? policy_evict_first()
                                                            : policy_evict_normal();
       const int ebase = un.expert * args.w_rows;
-      const int a_row0 = ebase + un.mt * 256 + 128 * (int)rank;
-      const int a_row1 = a_row0 + (args.w_rows >> 1);  // SwiGLU: the matching up rows
+      // SwiGLU: gate rows of a 256-feature tile, then the matching up rows; BF16 with two
+      // tiles: 256 consecutive rows of a 512-row tile per CTA
+      const int a_row0 = EPI == FUS_EPI_SWIGLU || NA == 1
+                             ? ebase + un.mt * 256 + 128 * (int)rank
+                             : ebase + un.mt * 512 + 256 * (int)rank;
+      const int a_row1 = EPI == FUS_EPI_SWIGLU ? a_row0 + (args.w_rows >> 1) : a_row0 + 128;
       const int b_row = pos0 + (int)rank * half;
       for (int i = 0; i < nk; ++i, ++c) {
         const int s = c % STAGES;
@@ -218,7 +225,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const int kk = i * kBK;
             const uint32_t a_dst = sA + s * Cfg::A_BYTES;
             tma_load_2d_pair(a_dst, tma_a, full_leader, kk, a_row0, pol_w);
-            if (EPI == FUS_EPI_SWIGLU)
+            if (NA == 2)
               tma_load_2d_pair(a_dst + kATileBytes, tma_a, full_leader, kk, a_row1, pol_w);
             tma_load_2d_pair(sB + s * Cfg::B_BYTES, tma_b, full_leader, kk % args.K, b_row,
                              pol_x);
@@ -261,7 +268,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
               for (int k = 0; k < kBK / 16; ++k) {
                 const uint64_t bdesc = sw128_desc(b_base + 32 * k);
                 tc_mma_bf16_pair(acc, sw128_desc(a_base + 32 * k), bdesc, idesc, (i | k) != 0);
-                if (EPI == FUS_EPI_SWIGLU)
+                if (NA == 2)
                   tc_mma_bf16_pair(acc + kPairBN, sw128_desc(a_base + kATileBytes + 32 * k),
                                    bdesc, idesc, (i | k) != 0);
               }
@@ -300,7 +307,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const bool out32 = EPI == FUS_EPI_BF16 && (G.flags & FUS_GEMM_OUT_F32);
       const int CH = out32 ? 16 : 32;
       const CUtensorMap* tmo = un.gi ? &to1 : &to0;
-      const int col0 = un.mt * 256 + 128 * (int)rank;  // this CTA's first output feature
+      constexpr bool kTwoOut = EPI == FUS_EPI_BF16 && NA == 2;  // two 128-feature outputs
+      // this CTA's first output feature
+      const int col0 = kTwoOut ? un.mt * 512 + 256 * (int)rank : un.mt * 256 + 128 * (int)rank;
       if (et == 0)
         *my_ok = mbar_wait_bounded(bar_acc_full + 8 * buf, use & 1u, abort_flag, args.status);
       named_bar_sync(bar_id, 128);
@@ -309,16 +318,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       for (int c0 = eg * CH; c0 < n_mma; c0 += kPEpiGroups * CH) {
         const bool two = !out32 && c0 + 16 < n_mma;  // second 16 columns (warp-uniform)
         uint8_t* stg = staging + (half_sel & 1u) * (Cfg::STAGING_BYTES / 2);
+        if (kTwoOut) {
+          // this chunk fills both halves: every earlier store has read its source first
+          stg = staging;
+          if (et == 0) bulk_wait_read_all();
+          named_bar_sync(bar_id, 128);
+        }
         uint32_t ra[16], rb[16], rc[16], rd[16];
         tmem_ld16_issue(lane_base + (uint32_t)c0, ra);
         if (two) tmem_ld16_issue(lane_base + (uint32_t)(c0 + 16), rc);
-        if (EPI == FUS_EPI_SWIGLU) {
+        if (NA == 2) {
           tmem_ld16_issue(lane_base + (uint32_t)(kPairBN + c0), rb);
           if (two) tmem_ld16_issue(lane_base + (uint32_t)(kPairBN + c0 + 16), rd);
         }
         tmem_ld_wait(ra);
         if (two) tmem_ld_wait(rc);
-        if (EPI == FUS_EPI_SWIGLU) {
+        if (NA == 2) {
           tmem_ld_wait(rb);
           if (two) tmem_ld_wait(rd);
         }
@@ -340,6 +355,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         };
         stage16(0, ra, rb);
         if (two) stage16(16, rc, rd);
+        if (kTwoOut) {  // the second weight tile's features into the other half
+          uint8_t* keep = stg;
+          stg = staging + Cfg::STAGING_BYTES / 2;
+          stage16(0, rb, rb);
+          if (two) stage16(16, rd, rd);
+          stg = keep;
+        }
         // the previous store (other half) must have read its source before anyone passes
         // this barrier into the next chunk, which refills that half. Rows past the map's
         // extent are clipped by the copy engine; rows past n_live inside the block are
@@ -349,6 +371,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         named_bar_sync(bar_id, 128);
         if (et == 0) {
           tma_store_2d(tmo, smem_u32(stg), col0, pos0 + c0);
+          if (kTwoOut)
+            tma_store_2d(tmo, smem_u32(staging + Cfg::STAGING_BYTES / 2), col0 + 128, pos0 + c0);
           bulk_commit();
         }
         ++half_sel;

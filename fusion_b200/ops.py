@@ -16,6 +16,7 @@ from . import _lib as L
 FUS_EPI_BF16, FUS_EPI_SWIGLU, FUS_EPI_F32 = 0, 1, 2
 GEMM_OUT_F32, GEMM_SWIGLU_EXACT, GEMM_W_STREAM, GEMM_MERGE, GEMM_NO_PERSIST = 0x1, 0x2, 0x4, 0x8, 0x10
 GEMM_NO_PAIR = 0x40
+GEMM_PAIR_NARROW = 0x80
 GEMM_SCALE_TOKEN = 0x20
 ERR_TIMEOUT, ERR_BAD_EXPERT, ERR_CAPACITY = 0x1, 0x2, 0x4
 

@@ -62,6 +62,10 @@ extern "C" {
 #define FUS_GEMM_NO_PAIR 0x40     /* (first group) no SM-pair (2-CTA cluster, M = 256)     */
                                   /* tiles; by default persistent launches with 256-token  */
                                   /* blocks and dense outputs use them                     */
+#define FUS_GEMM_PAIR_NARROW 0x80 /* (first group) FUS_EPI_BF16 SM-pair tiles of 256 rows  */
+                                  /* (one weight tile per CTA, TMEM double-buffered); by  */
+                                  /* default 512-row tiles (two weight tiles per CTA      */
+                                  /* share each staged token tile) when w_rows allows     */
 
 int fus_version(void);
 const char* fus_last_error(void);

@@ -227,7 +227,8 @@ def test_pair_tiles_ragged_experts(epi, layout):
     expert blocks holding 1 .. 256 live tokens (token boxes of 16 / 64 / 128 rows per
     CTA), with a dense second group (fp32 output on the down projection); and match an
     fp32 reference. Experts with two blocks (300, 257 and 511 tokens) and three (513), in
-    the reference layout (full block + remainder) and the balanced one."""
+    the reference layout (full block + remainder) and the balanced one; on the down
+    projection both the 512-row pair tiles (default) and the 256-row ones."""
     counts = [1, 17, 100, 130, 256, 300, 513, 40, 257, 511]
     E, bn = len(counts), 256
     ids = np.concatenate([np.full(c, e, np.int32) for e, c in enumerate(counts)])
@@ -265,7 +266,7 @@ def test_pair_tiles_ragged_experts(epi, layout):
         w_rows, K, n_out, epi_id, xin, xsh = H, I, H, ops.FUS_EPI_BF16, a, a_s
         fl = 0
     outs = []
-    for flag in (0, ops.GEMM_NO_PAIR, ops.GEMM_NO_PERSIST):
+    for flag in (0, ops.GEMM_PAIR_NARROW, ops.GEMM_NO_PAIR, ops.GEMM_NO_PERSIST):
         o = torch.zeros(cap, n_out, dtype=torch.bfloat16, device=DEV)
         # the shared group writes fp32 on the down projection (as the prefill block does)
         o_s = torch.zeros(T, n_out, dtype=torch.bfloat16 if epi == "swiglu" else torch.float32,

@@ -552,7 +552,8 @@ int launch_pair(const CUtensorMap* maps, const GemmArgs& a, long total, cudaStre
   long clusters = max_clusters > 0 ? max_clusters : num_sms() / 2;
   if (clusters > total) clusters = total;
   grouped_gemm_pair<EPI, NA><<<(int)(2 * clusters), kPThreads, Cfg::SMEM_BYTES, st>>>(
-      maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[4], maps[5], a);
+      maps[0], maps[1], maps[2], maps[3], maps[6], maps[7], maps[8], maps[9], maps[10], maps[11],
+      maps[4], maps[5], a);
   return check_launch("grouped_gemm_pair");
 }
 
@@ -720,7 +721,7 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
   }
   a.group_blocks = group_blocks;
 
-  CUtensorMap maps[10] = {};
+  CUtensorMap maps[12] = {};
   long units[2] = {0, 0};
   const int a_box_rows = (epilogue == FUS_EPI_SWIGLU && !mt2) ? 64 : 128;
   const int out_cols = epilogue == FUS_EPI_SWIGLU ? w_rows / 2 : w_rows;
@@ -815,6 +816,9 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
         if (!rc)
           rc = make_tmap_bf16_2d(&maps[8 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
                                  (uint64_t)G.ldx, kBK, 64);
+        if (!rc)
+          rc = make_tmap_bf16_2d(&maps[10 + g], G.x, (uint64_t)K, (uint64_t)G.x_rows,
+                                 (uint64_t)G.ldx, kBK, 96);
         if (rc) return rc;
         a.g[g].tma_store = 1;
       }
@@ -823,6 +827,7 @@ static int grouped_gemm_impl(const fus_gemm_group* groups, int ngroups, int w_ro
         maps[5] = maps[4];
         maps[7] = maps[6];
         maps[9] = maps[8];
+        maps[11] = maps[10];
       }
       const long ptotal = pu[0] + pu[1];
       if (ptotal > 0x7fffffffL) return set_error(FUS_E_UNSUPPORTED, "grid too large");

@@ -14,6 +14,9 @@
 //   BF16 (w2):    tile = 256 output features; one MMA per K step into 256 columns, and the
 //     two accumulator sets are double-buffered so the next tile's MMAs run under the drain.
 //
+// Token boxes per CTA are 16, 64, 96 or 128 rows (one TMA copy per stage, the smallest
+// that holds the CTA's half of the live rows: a ~150-token block moves 96 rows, not 128).
+//
 // Synchronisation: both CTAs' TMA loads of a stage complete on the LEADER's full barrier
 // (cp.async.bulk.tensor .cta_group::2, barrier addressed through the cluster window; no
 // multicast), whose expected byte count the leader posts for both. The leader's
@@ -129,6 +132,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                       const __grid_constant__ CUtensorMap tbs1,
                       const __grid_constant__ CUtensorMap tbm0,  // token box 64 rows
                       const __grid_constant__ CUtensorMap tbm1,
+                      const __grid_constant__ CUtensorMap tbw0,  // token box 96 rows
+                      const __grid_constant__ CUtensorMap tbw1,
                       const __grid_constant__ CUtensorMap to0,
                       const __grid_constant__ CUtensorMap to1,
                       const __grid_constant__ GemmArgs args) {
@@ -196,10 +201,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const int pos0 = un.blk * kPairBN;
       const int n_live = live_columns(G, pos0, kPairBN, lane);
       const int half = max(16, (n_live + 15) & ~15) / 2;  // token rows per CTA (multiple of 8)
-      const int bx = half <= 16 ? 16 : (half <= 64 ? 64 : 128);
+      // one box per stage, the smallest of 16 / 64 / 96 / 128 rows that holds the half
+      const int bx = half <= 16 ? 16 : half <= 64 ? 64 : half <= 96 ? 96 : 128;
       const CUtensorMap* tma_a = un.gi ? &ta1 : &ta0;
       const CUtensorMap* tma_b = bx == 128 ? (un.gi ? &tb1 : &tb0)
                                  : bx == 16 ? (un.gi ? &tbs1 : &tbs0)
+                                 : bx == 96 ? (un.gi ? &tbw1 : &tbw0)
                                             : (un.gi ? &tbm1 : &tbm0);
       // both CTAs' bytes land on the leader's barrier
       const uint32_t stage_tx = 2u * (uint32_t)(Cfg::A_BYTES + bx * kBK * 2);

@@ -159,7 +159,9 @@ int fus_moe_align_ex(const int* ids, int numel, int E, int block_m, int* sorted_
  * call on each device looks up the array's device address (cudaGetSymbolAddress) with
  * that device current; make that first call before any stream capture. All calls on a
  * device share the array: calls that may overlap on the GPU (different streams, no
- * ordering between them) race and corrupt each other's layout. */
+ * ordering between them) race and corrupt each other's layout. The looked-up address is
+ * kept for the life of the process: after cudaDeviceReset on a device it is stale, so do
+ * not call this entry again on that device. */
 int fus_moe_align_noalloc(const int* ids, int numel, int E, int block_m, int* sorted_ids,
                           int sorted_cap, int* expert_ids, int blocks_cap, int* ntp, void* stream,
                           int* status);

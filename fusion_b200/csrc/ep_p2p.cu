@@ -222,8 +222,8 @@ int launch_1cta(void (*kernel)(KArgs...), int pdl, void* stream, const char* wha
 
 // ---- the whole decode step on one rank (workspace layout) ----
 struct P2PStepLayout {
-  int R, n, rs_cap, rs_bcap, l_cap, l_bcap;
-  size_t off_x2, off_logits, off_rs, off_reids, off_rntp, off_slots, off_ls, off_leids, off_lntp,
+  int R, n, l_cap, l_bcap;
+  size_t off_x2, off_logits, off_slots, off_ls, off_leids, off_lntp,
       off_act, off_acts, off_y, off_ys, total;
 };
 
@@ -233,8 +233,6 @@ static bool p2p_layout(const fus_ep_p2p_desc* d, int T, P2PStepLayout& L) {
   const int H = b->H, I = b->I, E = b->E, K = b->topk;
   L.R = T * K;
   L.n = d->W * d->S;
-  L.rs_cap = (L.R + E * 15 + 15) / 16 * 16;  // route_small's layout over all experts (unused)
-  L.rs_bcap = L.rs_cap / 16;
   L.l_cap = (L.n + d->E_loc * 15 + 15) / 16 * 16;
   L.l_bcap = L.l_cap / 16;
   size_t o = 256;  // the front end's ticket sits at offset 0 and stays zero
@@ -245,9 +243,6 @@ static bool p2p_layout(const fus_ep_p2p_desc* d, int T, P2PStepLayout& L) {
   };
   L.off_x2 = take((size_t)T * H * 2);
   L.off_logits = take((size_t)T * E * 4);
-  L.off_rs = take((size_t)L.rs_cap * 4);
-  L.off_reids = take((size_t)L.rs_bcap * 4);
-  L.off_rntp = take(16);
   L.off_slots = take((size_t)L.R * 4);
   L.off_ls = take((size_t)L.l_cap * 4);
   L.off_leids = take((size_t)L.l_bcap * 4);
@@ -307,13 +302,12 @@ extern "C" int fus_ep_p2p_decode_forward(const fus_ep_p2p_desc* d, const void* h
   void* ys = at(L.off_ys);
   const bool shared = b->w13s != nullptr;
   int rc;
-  // 1 norm + router + top-k (its layout over all experts goes to scratch)
+  // 1 norm + router + top-k (block_m 0: no dispatch layout over all experts; the owners
+  // build theirs from what they receive)
   if ((rc = route_small_launch(h, r, b->gamma, b->eps, b->wa, b->nplanes, b->bias, T, H, E, K,
                                 b->routed_scale, b->renorm, b->n_group, b->topk_group, h1, x2,
-                                reinterpret_cast<float*>(at(L.off_logits)), topw, topi, 16,
-                                reinterpret_cast<int*>(at(L.off_rs)), L.rs_cap,
-                                reinterpret_cast<int*>(at(L.off_reids)), L.rs_bcap,
-                                reinterpret_cast<int*>(at(L.off_rntp)), done, nullptr, 0, stream,
+                                reinterpret_cast<float*>(at(L.off_logits)), topw, topi, 0,
+                                nullptr, 0, nullptr, 0, nullptr, done, nullptr, 0, stream,
                                 status)))
     return rc;
   // 2 rows + local expert ids into the owners' exchange buffers, flags raised

@@ -292,6 +292,11 @@ __global__ void __launch_bounds__(kRouteThreads)
     }
   }
   RT(__syncthreads(); if (threadIdx.x == 0) g_route_trace[4] = globaltimer_ns();)
+  if (a.block_m == 0) {  // no layout wanted (the expert-parallel step builds its own)
+    for (int i = tid; i < a.zero_n; i += kRouteThreads) a.zero[i] = 0;
+    if (tid == 0) *a.done = 0;  // re-arm the ticket
+    return;
+  }
   // dispatch layout over the T*topk flat indices (stable by flat index)
   const int numel = T * a.topk;
   for (int e = tid; e < 256; e += kRouteThreads) cnt[e] = 0;
@@ -357,7 +362,7 @@ int route_small_check(int T, int H, int E, int topk, int n_group, int topk_group
     return set_error(FUS_E_UNSUPPORTED, "route_small: n_group=%d topk_group=%d E=%d", n_group,
                      topk_group, E);
   if (T < 1 || T > kRouteMaxT || E < 2 || E > 256 || E % 2 || topk < 1 || topk > 16 ||
-      topk > E || T * topk > 256 || H % 8 || H <= 0 || H > 8192 || block_m < 1 ||
+      topk > E || T * topk > 256 || H % 8 || H <= 0 || H > 8192 || block_m < 0 ||
       (nplanes != 1 && nplanes != 3))
     return set_error(FUS_E_UNSUPPORTED, "route_small: T=%d E=%d topk=%d H=%d unsupported", T, E,
                      topk, H);
@@ -376,8 +381,8 @@ int route_small_launch(const void* h, const void* r, const void* gamma, float ep
     return rc;
   if (n_group < 1) n_group = 1;
   if (topk_group < 1) topk_group = 1;
-  if (!h || !r || !gamma || !wa || !h1 || !x2 || !logits || !topw || !topi || !sorted_ids ||
-      !expert_ids || !ntp || !done || (zero_n > 0 && !zero))
+  if (!h || !r || !gamma || !wa || !h1 || !x2 || !logits || !topw || !topi ||
+      (block_m > 0 && (!sorted_ids || !expert_ids || !ntp)) || !done || (zero_n > 0 && !zero))
     return set_error(FUS_E_INVALID, "route_small: null argument");
   if (!aligned16(h) || !aligned16(r) || !aligned16(gamma) || !aligned16(wa) || !aligned16(h1) ||
       !aligned16(x2))

@@ -169,10 +169,11 @@ int fus_moe_align_noalloc(const int* ids, int numel, int E, int block_m, int* so
 /* Decode front end in one launch (T <= 16): add_rmsnorm + fp32 router + top-k + dispatch
  * layout (replaces fus_add_rmsnorm + fus_router_logits + fus_router_topk +
  * fus_moe_align for small T). Every CTA normalises the T rows into shared memory and
- * computes the logits of two experts; the last CTA to finish selects the top-k and
- * builds the layout. `done` is an int that must be zero before the first call (each
- * call leaves it zero); `zero`/`zero_n` optionally names an int buffer the call clears
- * (the fused merge's counters). Requires E <= 256, E % 2 == 0, T*topk <= 256. */
+ * computes the logits of one expert; the last CTA to finish selects the top-k and
+ * builds the layout (block_m = 0: no layout; sorted_ids, expert_ids and ntp may then be
+ * NULL). `done` is an int that must be zero before the first call (each call leaves it
+ * zero); `zero`/`zero_n` optionally names an int buffer the call clears (the fused
+ * merge's counters). Requires E <= 256, E % 2 == 0, T*topk <= 256. */
 int fus_moe_route_small(const void* h, const void* r, const void* gamma, float eps, const void* wa,
                         int nplanes, const float* bias, int T, int H, int E, int topk,
                         float scale, int renorm, void* h1, void* x2, float* logits, float* topw,

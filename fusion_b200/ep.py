@@ -77,7 +77,16 @@ class ExpertParallelMoE:
         h1, x2, topw, topi = be.route(h, r)
         T, K = topi.shape
         W = self.W
-        plan = be.plan_dedup(topi, W, with_pair_pos=combine == "pairs")
+        ys = None
+        if hasattr(be, "plan_finish"):
+            # the counts travel to the host while the GPU runs the shared expert (queued
+            # behind the copy on the same stream), so the host's wait and the launches
+            # that follow it overlap GPU work
+            plan = be.plan_dedup(topi, W, with_pair_pos=combine == "pairs", defer=True)
+            ys = be.shared(x2)
+            be.plan_finish(plan)
+        else:
+            plan = be.plan_dedup(topi, W, with_pair_pos=combine == "pairs")
         counts = plan["counts"]  # [rows, pairs] per destination
         rows_out = [c[0] for c in counts]
         pairs_out = [c[1] for c in counts]
@@ -101,7 +110,8 @@ class ExpertParallelMoE:
             y = be.local_experts_return(recv_rows, recv_leid, recv_ret, rows_in, pairs_in)
             ret = torch.empty(sum(pairs_out), H, dtype=y.dtype, device=rows.device)
             self._a2a(ret, y, pairs_out, pairs_in)
-            ys = be.shared(x2)
+            if ys is None:
+                ys = be.shared(x2)
             out = be.merge_pairs(ret, plan["pair_pos"], topw, h1, ys)
         else:
             wts, pos = meta
@@ -113,7 +123,8 @@ class ExpertParallelMoE:
             ret = torch.empty(n_send + 1, H, dtype=part.dtype, device=rows.device)
             ret[n_send].zero_()
             self._a2a(ret[:n_send], part, rows_out, rows_in)
-            ys = be.shared(x2)
+            if ys is None:
+                ys = be.shared(x2)
             out = be.merge_dedup(ret, pos, h1, ys)
         return {"out": out, "h1": h1, "topw": topw, "topi": topi, "rows_in": n_in,
                 "pairs_in": sum(pairs_in)}
@@ -453,7 +464,10 @@ class CudaEPBackend:
         ops.moe_align(dest, W, 1, send_ids, eids, ntp)  # stable sort by destination
         return send_ids, leid, [int(v) for v in counts.tolist()]
 
-    def plan_dedup(self, topi, W: int, with_pair_pos: bool = True) -> dict:
+    def plan_dedup(self, topi, W: int, with_pair_pos: bool = True, defer: bool = False) -> dict:
+        """Send plan of the deduplicated dispatch. defer=True leaves the per-destination
+        counts on their way to the host (`plan_finish` reads them), so the caller can
+        queue more GPU work behind the copy before it waits."""
         T, K = topi.shape
         keys = torch.empty(T * W, dtype=torch.int32, device=self.dev)
         counts = torch.empty(2 * W, dtype=torch.int32, device=self.dev)
@@ -476,7 +490,25 @@ class CudaEPBackend:
             n2 = torch.zeros(1, dtype=torch.int32, device=self.dev)
             plan["pair_pos"] = torch.empty(T, K, dtype=torch.int32, device=self.dev)
             ops.moe_align(dest, W, 1, srt, e2, n2, pos_of=plan["pair_pos"])
-        c = counts.tolist()
+        plan["W"] = W
+        if defer:
+            host = torch.empty(2 * W, dtype=torch.int32, pin_memory=True)
+            host.copy_(counts, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            plan["_host"] = (host, ev)
+            return plan
+        return self.plan_finish(plan, counts)
+
+    def plan_finish(self, plan: dict, counts=None) -> dict:
+        """The host side of the plan: per destination [rows, pairs]."""
+        W = plan["W"]
+        if counts is None:
+            host, ev = plan.pop("_host")
+            ev.synchronize()
+            c = host.tolist()
+        else:
+            c = counts.tolist()
         plan["counts"] = [[c[d], c[W + d]] for d in range(W)]
         return plan
 

@@ -249,12 +249,20 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     pk = traffic.peaks()
 
-    def decode_step(T: int):
-        # p2p: the whole step as one library call (PDL-chained, NVLink exchange);
-        # nccl: the Python-composed step with all_to_all; both replayed from a CUDA graph
-        if args.ep_exchange == "p2p":
+    def fixed_slots(T: int) -> bool:
+        # the fixed-slot exchange (no host synchronisation, graph-replayed) serves batches
+        # whose slot blocks fit its single-CTA dispatch and combine kernels
+        return T * dims.topk <= 1024 and world * T * dims.topk <= 4096
+
+    def decode_step(T: int, zipf: bool = False):
+        # p2p: T <= 16, the whole step as one library call (PDL-chained, NVLink exchange);
+        # larger fixed-slot batches: the Python-composed step over the same NVLink
+        # exchange; nccl: the Python-composed step with all_to_all; all replayed from a
+        # CUDA graph
+        if args.ep_exchange == "p2p" and T <= 16 and not zipf:
             return EPDecodeStep(be, T).capture()
-        return EPDecodeGraph(ep, T, dims.H, "cuda", exchange="nccl")
+        return EPDecodeGraph(ep_z if zipf else ep, T, dims.H, "cuda",
+                             exchange=args.ep_exchange)
 
     def inputs(T: int, tag: int = 0):
         return synth.make_inputs(SEED * 1000 + T + rank + tag, T, dims, "cuda")
@@ -263,14 +271,14 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
     def parity() -> dict:
         full = synth.make_block_weights(SEED, dims, "cuda")
         res = {}
-        for name, T, zipf in (("decode_T1", HEADLINE_T, False), ("prefill_T256", 256, False),
-                              ("prefill_T2048_zipf", 2048, True)):
+        for name, T, zipf in (("decode_T1", HEADLINE_T, False), ("fixed_slots_T32", 32, False),
+                              ("prefill_T256", 256, False), ("prefill_T2048_zipf", 2048, True)):
             blk = MoEBlock(full["gamma"], full["gate_w"], zb if zipf else full["bias"],
                            full["w13"], full["w2"], full["w13s"], full["w2s"])
             h, r = inputs(T)
             ref = blk(h, r)
-            if T <= 16:
-                g = decode_step(T)
+            if fixed_slots(T):
+                g = decode_step(T, zipf)
                 g.h.copy_(h)
                 g.r.copy_(r)
                 out = g.replay().clone()
@@ -302,9 +310,9 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
         if rank == 0:
             print(f"[bench ep{world}] T={T}/rank zipf={zipf}", file=sys.stderr, flush=True)
         h, r = inputs(T)
-        small = T <= 16 and not zipf
+        small = fixed_slots(T)
         if small:  # fixed-slot exchange recorded in a CUDA graph (no host sync)
-            g = decode_step(T)
+            g = decode_step(T, zipf)
             g.h.copy_(h)
             g.r.copy_(r)
             run = g.replay
@@ -397,9 +405,11 @@ def run_ep(args, world: int, rank: int, local: int, barrier, max_over_ranks,
             "data": "synthetic (seeded Irwin-Hall normals, GLM-5.2 shapes, random-init weights)",
             "config": headline_config(world),
             "details": {"experts_per_gpu": dims.E // world,
-                        "timing": f"T<=16: fixed-slot EP step ({exch}) replayed from a "
-                                  "CUDA graph; larger T: eager EP step (NCCL all_to_all, "
-                                  "deduplicated dispatch); CUDA events, max over ranks"},
+                        "timing": f"T*topk <= 1024 and W*T*topk <= 4096: fixed-slot EP "
+                                  f"step ({exch}) replayed from a CUDA graph (one library "
+                                  "call at T <= 16); larger T: eager EP step (NCCL "
+                                  "all_to_all, deduplicated dispatch); CUDA events, max "
+                                  "over ranks"},
             "parity": par,
             "parity_ok": all(v["ok"] for v in par.values()),
             "us_per_block": head["us_per_block"],

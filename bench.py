@@ -69,17 +69,22 @@ def cpu_reference(T: int, steps: int, warmup: int, budget_s: float = 60.0,
                   ranks: int = 1) -> dict:
     """The reference path on the host cores: ``ranks`` ranks' worth of T tokens each (the
     GPU arm's inputs: rank g's tokens are seed SEED*1000 + T + g), every step one block
-    over all of them. Inputs come from the numpy restatement of the generator, so this
-    arm loads no part of the CUDA library."""
+    over all of them, through ``oracle.reference_torch`` (the reference's own torch CPU
+    operations in its order, bit-identical to glm52_h200/reference.py and as fast).
+    Inputs come from the numpy restatement of the generator, so this arm loads no part
+    of the CUDA library."""
     import numpy as np
+    import torch
     from threadpoolctl import threadpool_limits
 
     from oracle import reference_np as O
+    from oracle import reference_torch as RT
     from oracle import synth_np as S
 
     cores = os.cpu_count() or 1
     # torchrun exports OMP_NUM_THREADS=1; the reference arm uses every host core
     threadpool_limits(cores)
+    torch.set_num_threads(cores)
     h = np.concatenate([S.make("h", (T, H), SEED * 1000 + T + g) for g in range(ranks)])
     r = np.concatenate([S.make("r", (T, H), SEED * 1000 + T + g) for g in range(ranks)])
     gamma = S.make("gamma", (H,), SEED)
@@ -88,17 +93,21 @@ def cpu_reference(T: int, steps: int, warmup: int, budget_s: float = 60.0,
     x2, _ = O.add_rmsnorm(h, r, gamma)
     _, _, ids = O.router(x2, gw, bias)
     used = sorted(set(ids.flatten().tolist()))
+    bf = torch.bfloat16
     # weights resident in host memory before timing, as they are in HBM on the GPU side
-    w13 = {e: S.expert_weight("w13", e, H, I, SEED) for e in used}
-    w2 = {e: S.expert_weight("w2", e, H, I, SEED) for e in used}
-    w13s = S.make("w13s", (2 * I, H), SEED)
-    w2s = S.make("w2s", (H, I), SEED)
+    w13 = {e: torch.from_numpy(S.expert_weight("w13", e, H, I, SEED)).to(bf) for e in used}
+    w2 = {e: torch.from_numpy(S.expert_weight("w2", e, H, I, SEED)).to(bf) for e in used}
+    w13s = torch.from_numpy(S.make("w13s", (2 * I, H), SEED)).to(bf)
+    w2s = torch.from_numpy(S.make("w2s", (H, I), SEED)).to(bf)
+    h_t, r_t = torch.from_numpy(h).to(bf), torch.from_numpy(r).to(bf)
+    gamma_t = torch.from_numpy(gamma).to(bf)
+    gw_t, bias_t = torch.from_numpy(gw), torch.from_numpy(bias)
     T = T * ranks
 
     def step():
-        O.moe_block(h, r, gamma, gw, bias, w13.__getitem__, w2.__getitem__, w13s, w2s, E)
+        RT.moe_block(h_t, r_t, gamma_t, gw_t, bias_t, w13, w2, w13s, w2s, E)
 
-    for _ in range(max(1, min(warmup, 2))):
+    for _ in range(max(2, min(warmup, 3))):
         step()
     times = []
     t_end = time.perf_counter() + budget_s
@@ -117,7 +126,8 @@ def cpu_reference(T: int, steps: int, warmup: int, budget_s: float = 60.0,
         "ms_per_step": per * 1e3,
         "steps_timed": len(times),
         "sample": f"T={T}: full block (norm, fp32 router, {len(used)} routed + 1 shared "
-                  f"expert MLPs, merge) per step, {len(times)} steps, numpy fp32 BLAS",
+                  f"expert MLPs, merge) per step, {len(times)} steps, the reference's torch "
+                  f"CPU ops (bf16 linears, per-expert loop) restated in oracle/reference_torch.py",
     }
 
 
@@ -626,7 +636,7 @@ def main() -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_reference(HEADLINE_T, steps=10, warmup=1, budget_s=30.0)
+        cpu = cpu_reference(HEADLINE_T, steps=300, warmup=3, budget_s=15.0)
 
     if rank == 0:
         line = {

@@ -599,16 +599,17 @@ def main() -> None:
 
     # ---- e2e through the public API with pinned host buffers ----
     T = HEADLINE_T
-    hh, rh = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cpu")
-    hh, rh = hh.pin_memory(), rh.pin_memory()
+    hh0, rh0 = synth.make_inputs(SEED * 1000 + T + rank, T, dims, "cpu")
+    # h and r side by side in one pinned buffer: one host-to-device copy per step
+    hr_h = torch.stack([hh0, rh0]).pin_memory()
+    hh, rh = hr_h[0], hr_h[1]
     out_h = torch.empty(T, dims.H, dtype=torch.bfloat16).pin_memory()
-    hd = torch.empty(T, dims.H, dtype=torch.bfloat16, device="cuda")
-    rd = torch.empty_like(hd)
+    hr_d = torch.empty(2, T, dims.H, dtype=torch.bfloat16, device="cuda")
+    hd, rd = hr_d[0], hr_d[1]
     outs = blk.alloc_outputs(T)
 
     def e2e_step():
-        hd.copy_(hh, non_blocking=True)
-        rd.copy_(rh, non_blocking=True)
+        hr_d.copy_(hr_h, non_blocking=True)
         blk.forward(hd, rd, outs)
         out_h.copy_(outs.out, non_blocking=True)
 

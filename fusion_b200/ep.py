@@ -302,8 +302,9 @@ class EPDecodeStep:
             raise ValueError("ep_p2p_decode: bad sizes")
         self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=be.dev)
         bf = torch.bfloat16
-        self.h = torch.zeros(T, be.H, dtype=bf, device=be.dev)
-        self.r = torch.zeros_like(self.h)
+        # h and r as the two halves of one buffer: a caller fills both with one copy
+        self.hr = torch.zeros(2, T, be.H, dtype=bf, device=be.dev)
+        self.h, self.r = self.hr[0], self.hr[1]
         self.out = torch.empty_like(self.h)
         self.h1 = torch.empty_like(self.h)
         self.topw = torch.empty(T, be.topk, dtype=torch.float32, device=be.dev)
@@ -355,8 +356,9 @@ class EPDecodeGraph:
 
     def __init__(self, ep: ExpertParallelMoE, T: int, H: int, device, exchange: str = "p2p"):
         self.ep = ep
-        self.h = torch.zeros(T, H, dtype=torch.bfloat16, device=device)
-        self.r = torch.zeros_like(self.h)
+        # h and r as the two halves of one buffer: a caller fills both with one copy
+        self.hr = torch.zeros(2, T, H, dtype=torch.bfloat16, device=device)
+        self.h, self.r = self.hr[0], self.hr[1]
         self.x = None
         if exchange == "p2p":
             self.x = P2PExchange(T * ep.be.topk, H, device, ep.group)

@@ -34,14 +34,14 @@ def add_rmsnorm(x, residual, w, eps: float = RMS_NORM_EPS):
 
 
 def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
-    """reference.py:73-86: silu(gate) * up in fp32, result in the input dtype."""
+    """reference.py:73-77: silu(gate) * up in fp32, result in the input dtype."""
     d = x.shape[-1] // 2
     g, u = x[..., :d].float(), x[..., d:].float()
     return (F.silu(g) * u).to(x.dtype)
 
 
 def router(x, gate_w, bias, topk: int = TOPK, scale: float = ROUTED_SCALING_FACTOR):
-    """reference.py:138-176 with n_group = 1: fp32 logits, sigmoid, bias only in the
+    """reference.py:138-173 with n_group = 1: fp32 logits, sigmoid, bias only in the
     choice, top-k, renormalised weights times the scaling factor."""
     logits = F.linear(x.float(), gate_w.float())
     scores = logits.sigmoid()
